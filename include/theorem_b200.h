@@ -1,0 +1,132 @@
+/* theorem_b200.h -- C ABI of the B200 (sm_100a) Theorem forward hot path.
+ *
+ * Four ops, each replacing one `custom_kernel` of the reference
+ * (yhinai/Theorem, `kernels/<op>/kernel.py`). All pointers are device
+ * pointers to dense, contiguous tensors in the layouts documented per entry
+ * point; sizes are element counts. Every call is asynchronous on `stream`
+ * (NULL = the legacy default stream), allocates nothing, never mutates its
+ * inputs, and returns a thm_status. A CUDA error of the launch itself is
+ * reported as THM_ERR_CUDA; an in-kernel wait that ran out of time is
+ * reported later through thm_get_device_status().
+ *
+ * No CPU fallback exists: without a B200-class device the entry points
+ * return THM_ERR_CUDA / THM_ERR_UNSUPPORTED.
+ */
+#ifndef THEOREM_B200_H_
+#define THEOREM_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t / CUstream. */
+typedef struct CUstream_st* thm_stream_t;
+
+typedef enum {
+  THM_OK = 0,
+  THM_ERR_INVALID = 1,     /* bad shape / size / null pointer */
+  THM_ERR_UNSUPPORTED = 2, /* valid for the reference but not built here (e.g. K=96) */
+  THM_ERR_ALIGNMENT = 3,   /* pointer not 16-byte aligned */
+  THM_ERR_CUDA = 4,        /* CUDA launch / runtime error */
+  THM_ERR_TIMEOUT = 5,     /* an in-kernel bounded wait gave up (device status) */
+  THM_ERR_NO_DRIVER = 6    /* driver entry point (tensor maps) unavailable */
+} thm_status;
+
+typedef enum { THM_F32 = 0, THM_BF16 = 1 } thm_dtype;
+typedef enum { THM_LAYOUT_BDS = 0, THM_LAYOUT_BSD = 1 } thm_conv_layout;
+typedef enum { THM_ACT_NONE = 0, THM_ACT_SILU = 1 } thm_activation;
+
+/* ---------------------------------------------------------------------------
+ * causal_conv1d -- replaces kernels/causal_conv1d/kernel.py:170-230
+ * (custom_kernel; Triton causal_conv1d_kernel :44-117).
+ *
+ *   out[b,d,t] = act(bias[d] + sum_{k<W} weight[d,k] * x[b,d,t-W+1+k]),
+ *   x[...,t<0] = 0.
+ *
+ * layout THM_LAYOUT_BDS: x, out [B, D, S] (the reference layout, fp32 only).
+ * layout THM_LAYOUT_BSD: x, out [B, S, D] channel-last (fp32 or bf16), as the
+ *   gated-DeltaNet chain produces them; D % 8 == 0.
+ * weight [D, W] and bias [D] are fp32. 1 <= W <= 64 (BDS: W <= 8, BSD:
+ * W in {2,3,4} take the unrolled fast paths).
+ * l2norm_group (BSD only): 0, or G in {32,64,128,256}: after the
+ *   activation every run of G consecutive channels of a time step is scaled
+ *   by 1/sqrt(sum of squares + 1e-6) (the chain's q/k L2 norm over a head).
+ * ------------------------------------------------------------------------- */
+int thm_causal_conv1d_fwd(const void* x, const float* weight, const float* bias, void* out, int B, int D,
+                          int S, int W, int layout, int dtype, int activation, int l2norm_group,
+                          thm_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * recompute_w_u -- replaces kernels/recompute_w_u/kernel.py:192-248
+ * (_launch / custom_kernel; Triton recompute_w_u_kernel :73-186).
+ *
+ * Per 64-token chunk:  w = A (k * beta * exp(g)),  u = A (v * beta).
+ *   k [B,T,H,K], v [B,T,H,V] in `dtype`; beta, g [B,T,H] fp32;
+ *   A [B,T,H,64] fp32 (row t of its chunk's matrix at position t);
+ *   w [B,T,H,K], u [B,T,H,V] written in `dtype`.
+ * a_mode  0: A is read from `A` (the reference contract).
+ * a_mode -1: A is computed in-kernel as (I - M)^-1 (the reference's upstream
+ *            producer, kernels/recompute_w_u/reference.py:48-91),
+ * a_mode +1: A = (I + M)^-1 (gated DeltaNet), with
+ *            M = strict_tril(beta_i k_i.k_j exp(g_i - g_j)); `A` is ignored and
+ *            may be NULL; if A_out != NULL the computed A is stored there fp32.
+ * T % 64 == 0; K in {64, 128}; V in {64, 128}.
+ * ------------------------------------------------------------------------- */
+int thm_recompute_w_u_fwd(const void* k, const void* v, const float* beta, const float* A, const float* g,
+                          void* w, void* u, float* A_out, int B, int T, int H, int K, int V, int dtype,
+                          int a_mode, thm_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * chunk_fwd_h -- replaces kernels/chunk_fwd_h/kernel.py:141-191
+ * (custom_kernel; Triton chunk_fwd_h_kernel :61-138).
+ *
+ * mode 0 (reference): state = state*exp(g_end) + k_c^T (v_c * exp(g_end-g_c));
+ *   h[b,c,h] = state AFTER chunk c.  `w`, `h0`, `v_new`, `final_state` must be
+ *   NULL.
+ * mode 1 (gated delta rule): with h_c the state entering chunk c (h_0 = h0,
+ *   or 0 when h0 == NULL):
+ *     v_new_c = u_c - w_c h_c
+ *     h_{c+1} = exp(g_last) h_c + (k_c * exp(g_last - g_c))^T v_new_c
+ *   h[b,c,h] = h_c (state BEFORE chunk c); `v` is u; v_new (optional)
+ *   [B,T,H,V] in `dtype`; final_state (optional) [B,H,K,V] fp32 = h_NT.
+ * k, w [B,T,H,K], v [B,T,H,V] in `dtype`; g [B,T,H] fp32;
+ * h [B,T/64,H,K,V] fp32; h0 [B,H,K,V] fp32.
+ * T % 64 == 0; K in {64, 128}; V in {64, 128}.
+ * ------------------------------------------------------------------------- */
+int thm_chunk_fwd_h_fwd(const void* k, const void* w, const void* v, const float* g, const float* h0,
+                        float* h, void* v_new, float* final_state, int B, int T, int H, int K, int V,
+                        int dtype, int mode, thm_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * chunk_fwd_o -- replaces kernels/chunk_fwd_o/kernel.py:146-212
+ * (custom_kernel; Triton _chunk_fwd_o_kernel :52-136).
+ *
+ *   o = scale * ( tril_{s<=t}((q k^T) * exp(g_t - g_s)) v + (q * exp(g)) h[c] )
+ * q, k [B,T,H,K], v [B,T,H,V], o [B,T,H,V] in `dtype`; g [B,T,H] fp32;
+ * h [B,T/64,H,K,V] fp32 (used as given for chunk c).
+ * T % 64 == 0; K in {64, 128}; V % 64 == 0, V <= 512.
+ * ------------------------------------------------------------------------- */
+int thm_chunk_fwd_o_fwd(const void* q, const void* k, const void* v, const float* g, const float* h, void* o,
+                        float scale, int B, int T, int H, int K, int V, int dtype, thm_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Utilities
+ * ------------------------------------------------------------------------- */
+/* Human-readable name of a thm_status. */
+const char* thm_status_string(int status);
+
+/* Reads (and, if reset != 0, clears) the device status word on the current
+ * device: THM_OK, or the first in-kernel error (THM_ERR_TIMEOUT) recorded by
+ * any kernel of this library since the last reset. Synchronizes the device. */
+int thm_get_device_status(int* device_status, int reset);
+
+/* ABI version: (major << 16) | minor. */
+int thm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* THEOREM_B200_H_ */

@@ -1,0 +1,57 @@
+"""CPU checks of the C ABI: the library loads and exports every entry point the
+header declares; status strings resolve. No kernel is launched."""
+import re
+from pathlib import Path
+
+import pytest
+
+from theorem_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "theorem_b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(thm_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_is_built():
+    assert _lib.LIB_PATH.exists(), "run python -m theorem_b200.build"
+
+
+def test_every_declared_symbol_is_exported():
+    lib = _lib.load()
+    syms = declared_symbols()
+    assert len(syms) >= 7
+    for s in syms:
+        assert hasattr(lib, s), f"{s} declared in include/theorem_b200.h but not exported"
+
+
+def test_binding_covers_header():
+    assert set(declared_symbols()) == set(_lib.exported_symbols())
+
+
+@pytest.mark.parametrize("code", range(0, 8))
+def test_status_strings(code):
+    s = _lib.status_string(code)
+    assert s.startswith("THM_")
+
+
+def test_status_mapping_raises_reference_exception_classes():
+    with pytest.raises(AssertionError):
+        _lib.check(_lib.THM_ERR_INVALID, "x")
+    with pytest.raises(AssertionError):
+        _lib.check(_lib.THM_ERR_UNSUPPORTED, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.THM_ERR_TIMEOUT, "x")
+    _lib.check(_lib.THM_OK, "x")
+
+
+def test_invalid_arguments_rejected_without_gpu():
+    """Argument validation happens on the host before any CUDA call."""
+    lib = _lib.load()
+    # W = 0 is invalid; empty tensors are a no-op that never touches the device.
+    assert lib.thm_causal_conv1d_fwd(None, None, None, None, 1, 1, 1, 0, 0, 0, 0, 0, None) == _lib.THM_ERR_INVALID
+    assert lib.thm_causal_conv1d_fwd(None, None, None, None, 0, 8, 8, 4, 0, 0, 0, 0, None) == _lib.THM_OK
+    assert lib.thm_causal_conv1d_fwd(None, None, None, None, 1, 8, 8, 4, 7, 0, 0, 0, None) == _lib.THM_ERR_INVALID

@@ -1,0 +1,113 @@
+"""GPU parity: causal_conv1d through the C ABI vs the reference fixtures and the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops as orc
+from tests import golden_util as gu
+from tests.harness import assert_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _custom(data):
+    from theorem_b200.kernels.causal_conv1d import custom_kernel
+    return custom_kernel(data)
+
+
+@pytest.mark.parametrize("idx,shape", gu.cases("causal_conv1d"))
+def test_dropin_matches_reference_fixture(idx, shape):
+    """eval.py-style check (task.yml rtol=atol=1e-2) plus the north star's fp32
+    bar: |diff| <= 1e-4 against the float64 oracle."""
+    x, w, b = gu.regenerate("causal_conv1d", shape)
+    out = _custom((x.to(DEV), w.to(DEV), b.to(DEV)))
+    assert out.dtype == torch.float32 and out.shape == x.shape
+    rtol, atol = gu.tolerances("causal_conv1d")
+    gu.compare("causal_conv1d", idx, "out", out, rtol, atol)
+    gu.compare("causal_conv1d", idx, "out", out, 1e-4, 1e-4)
+    ref = torch.from_numpy(orc.causal_conv1d(x, w, b))
+    assert_close(out.cpu().double(), ref, 1e-4, 1e-4, "oracle")
+
+
+def test_dropin_does_not_mutate_inputs():
+    x, w, b = (t.to(DEV) for t in gu.regenerate("causal_conv1d", dict(B=2, D=64, S=256, W=4, seed=1)))
+    xs, ws, bs = x.clone(), w.clone(), b.clone()
+    _custom((x, w, b))
+    assert torch.equal(x, xs) and torch.equal(w, ws) and torch.equal(b, bs)
+
+
+def _baseline_conv_inputs(B, D, S, W, seed, device=DEV):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(B, D, S, generator=g)
+    w = torch.randn(D, W, generator=g) * 0.5          # N(0, 1/4)
+    b = torch.randn(D, generator=g) * (0.1 ** 0.5)     # N(0, 0.1)
+    return x, w, b
+
+
+def test_config1_silu_fp32_within_1em4():
+    """B1 D2560 S4096 W4 + SiLU, fp32, elementwise vs the oracle."""
+    from theorem_b200 import ops
+    x, w, b = _baseline_conv_inputs(1, 2560, 4096, 4, 0)
+    out = ops.causal_conv1d(x.to(DEV), w.to(DEV), b.to(DEV), activation="silu")
+    ref = orc.causal_conv1d(x, w, b, "silu")
+    diff = np.abs(out.cpu().double().numpy() - ref)
+    assert diff.max() <= 1e-4
+    big = np.abs(ref) > 1e-2
+    assert (diff[big] / np.abs(ref[big])).max() <= 1e-4
+
+
+@pytest.mark.parametrize("W", [1, 2, 3, 4, 5, 6, 7, 8, 9, 13])
+@pytest.mark.parametrize("S", [1, 3, 4, 12, 37, 64, 132])
+def test_bds_edge_sizes(W, S):
+    from theorem_b200 import ops
+    x, w, b = _baseline_conv_inputs(2, 24, S, W, 100 * W + S)
+    for act in (None, "silu"):
+        out = ops.causal_conv1d(x.to(DEV), w.to(DEV), b.to(DEV), activation=act)
+        ref = torch.from_numpy(orc.causal_conv1d(x, w, b, act))
+        assert_close(out.cpu().double(), ref, 1e-5, 1e-5, f"W={W} S={S} act={act}")
+
+
+def test_bds_misaligned_view_uses_scalar_path():
+    from theorem_b200 import ops
+    x, w, b = _baseline_conv_inputs(1, 16, 65, 4, 5)
+    base = torch.zeros(16 * 65 + 1, device=DEV)
+    xv = base[1:].view(1, 16, 65)
+    xv.copy_(x.to(DEV))
+    out = ops.causal_conv1d(xv, w.to(DEV), b.to(DEV))
+    assert_close(out.cpu().double(), torch.from_numpy(orc.causal_conv1d(x, w, b)), 1e-5, 1e-5)
+
+
+def test_empty_batch():
+    from theorem_b200 import ops
+    x = torch.empty(0, 8, 16, device=DEV)
+    w = torch.randn(8, 4, device=DEV)
+    b = torch.randn(8, device=DEV)
+    assert ops.causal_conv1d(x, w, b).shape == (0, 8, 16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("W", [2, 3, 4, 6])
+@pytest.mark.parametrize("G", [0, 64, 128])
+def test_channel_last_silu_l2norm(dtype, W, G):
+    """Chain front-end: [B,S,D] conv + SiLU (+ per-head L2 norm) in fp32 / bf16."""
+    from theorem_b200 import ops
+    B, S, D = 2, 77, 256
+    g = torch.Generator().manual_seed(W * 7 + G)
+    x = torch.randn(B, S, D, generator=g).to(dtype)
+    w = torch.randn(D, W, generator=g) * 0.5
+    b = torch.randn(D, generator=g) * 0.3
+    out = ops.causal_conv1d(x.to(DEV), w.to(DEV), b.to(DEV), activation="silu", layout="bsd", l2norm_group=G)
+    ref = orc.causal_conv1d(x.float(), w, b, "silu", layout="bsd")
+    if G:
+        ref = orc.l2norm(ref.reshape(B, S, D // G, G)).reshape(B, S, D)
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert out.dtype == dtype
+    assert_close(out.float().cpu().double(), torch.from_numpy(ref), tol, tol, f"{dtype} W={W} G={G}")
+
+
+def test_misaligned_channel_last_rejected():
+    from theorem_b200 import ops
+    x = torch.zeros(1, 4, 13 * 8, device=DEV)[..., :-8]  # D = 96 but row stride breaks contiguity
+    with pytest.raises(AssertionError):
+        ops.causal_conv1d(x, torch.zeros(96, 4, device=DEV), torch.zeros(96, device=DEV), layout="bsd")

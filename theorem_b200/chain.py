@@ -1,0 +1,70 @@
+"""Gated-DeltaNet layer forward built from the four C-ABI ops.
+
+The reference runs its three DeltaNet ops only separately, each on its own
+random inputs (kernels/*/reference.py); its docs compose them as
+recompute_w_u -> chunk_fwd_h -> chunk_fwd_o (docs/ARCHITECTURE.md:200-235)
+behind a Mamba-2 causal conv. This module chains them the gated-DeltaNet way:
+
+    q = l2norm(silu(conv(xq)))   k = l2norm(silu(conv(xk)))   v = silu(conv(xv))
+    A = (I + strict_tril(beta_i k_i.k_j e^{g_i-g_j}))^-1        (in-kernel)
+    w = A (k beta e^g),  u = A (v beta)
+    h_c = state entering chunk c (h_0 = h0); v_new = u - w h_c;
+    h_{c+1} = e^{g_last} h_c + (k e^{g_last - g})^T v_new
+    o = scale (tril(q k^T * e^{g_t - g_s}) v_new + (q e^g) h_c)
+
+Inputs xq, xk, xv are channel-last [B, T, H*K] (bf16 or fp32); beta and g
+[B, T, H] fp32 (g already the within-chunk cumulative gate). Intermediates
+(q, k, v, w, u, v_new in the input dtype; h fp32 [B, T/64, H, K, V]) are kept
+in buffers reused across calls with the same shape.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+
+class GatedDeltaNetForward:
+    """Callable layer forward; holds the depthwise conv weights [H*K, W] / [H*V, W]."""
+
+    def __init__(self, H: int, K: int, V: int, conv_weights, conv_biases, activation: str = "silu",
+                 scale: float | None = None):
+        assert len(conv_weights) == 3 and len(conv_biases) == 3, "q, k, v conv weights and biases"
+        self.H, self.K, self.V = H, K, V
+        self.wq, self.wk, self.wv = (w.contiguous().float() for w in conv_weights)
+        self.bq, self.bk, self.bv = (b.contiguous().float() for b in conv_biases)
+        self.activation = activation
+        self.scale = K ** -0.5 if scale is None else float(scale)
+        self._buf: dict = {}
+
+    def _buffers(self, xq, xv, B, T):
+        key = (B, T, xq.dtype, xq.device)
+        if self._buf.get("key") != key:
+            H, K, V = self.H, self.K, self.V
+            dev, dt = xq.device, xq.dtype
+            self._buf = dict(
+                key=key,
+                q=torch.empty(B, T, H, K, device=dev, dtype=dt),
+                k=torch.empty(B, T, H, K, device=dev, dtype=dt),
+                v=torch.empty(B, T, H, V, device=dev, dtype=dt),
+                w=torch.empty(B, T, H, K, device=dev, dtype=dt),
+                u=torch.empty(B, T, H, V, device=dev, dtype=dt),
+                h=torch.empty(B, T // 64, H, K, V, device=dev, dtype=torch.float32),
+            )
+        return self._buf
+
+    def __call__(self, xq, xk, xv, beta, g, h0=None, out=None, final_state: bool = True):
+        B, T, Dq = xq.shape
+        H, K, V = self.H, self.K, self.V
+        assert Dq == H * K and xk.shape == xq.shape and xv.shape == (B, T, H * V)
+        assert T % 64 == 0, "T must be a multiple of the chunk length 64"
+        bf = self._buffers(xq, xv, B, T)
+        q, k, v = bf["q"], bf["k"], bf["v"]
+        ops.causal_conv1d(xq, self.wq, self.bq, self.activation, "bsd", K, out=q.view(B, T, H * K))
+        ops.causal_conv1d(xk, self.wk, self.bk, self.activation, "bsd", K, out=k.view(B, T, H * K))
+        ops.causal_conv1d(xv, self.wv, self.bv, self.activation, "bsd", 0, out=v.view(B, T, H * V))
+        w, u = ops.recompute_w_u(k, v, beta, None, g, a_mode=1, w=bf["w"], u=bf["u"])
+        h, v_new, fin = ops.chunk_fwd_h(k, u, g, w=w, h0=h0, mode=1, want_v_new=True, want_final=final_state,
+                                        h=bf["h"], v_new=v)
+        o = ops.chunk_fwd_o(q, k, v_new, g, h, self.scale, o=out)
+        return o, fin

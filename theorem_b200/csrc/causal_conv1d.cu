@@ -1,0 +1,369 @@
+// causal_conv1d.cu -- depthwise causal 1-D convolution (Mamba-2 style).
+//
+// Replaces the reference's Triton kernel (kernels/causal_conv1d/kernel.py:44-117)
+// and its launcher (:170-230). Pure HBM streaming: every input element is
+// read from DRAM once and every output written once; the W-1 halo is re-read
+// from L1 (BDS) or carried in registers (BSD).
+//
+//   out[b,d,t] = act(bias[d] + sum_{k<W} weight[d,k] * x[b,d,t-W+1+k])
+//
+// BDS ([B,D,S], S contiguous, fp32): one thread = 8 consecutive outputs of a
+//   row, float4 loads/stores; the halo is the previous one or two float4 of
+//   the same row (L1 hits).
+// BSD ([B,S,D], D contiguous, fp32/bf16): one thread = 8 consecutive channels
+//   x TT consecutive time steps; 16-byte (bf16) or 2x16-byte (fp32) loads,
+//   the W-1 previous rows held in registers; optional SiLU and per-group L2
+//   norm (warp shuffles over G/8 lanes) fused into the store.
+#include <cuda_bf16.h>
+
+#include "host_util.h"
+#include "sm100.cuh"
+
+THM_DEFINE_STATUS(g_status_conv)
+
+namespace thm {
+namespace conv {
+
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// ---------------------------------------------------------------------------
+// BDS, fp32, S % 4 == 0, W <= 8
+// ---------------------------------------------------------------------------
+template <int W, bool SILU>
+__global__ void __launch_bounds__(256) conv_bds_vec8(const float* __restrict__ x, const float* __restrict__ w,
+                                                     const float* __restrict__ bias, float* __restrict__ out,
+                                                     int D, int S, long long nseg_total, int nseg_row) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nseg_total) return;
+  const long long row = i / nseg_row;
+  const int seg = (int)(i - row * nseg_row);
+  const int d = (int)(row % D);
+  const int t0 = seg * 8;
+  const float* xr = x + row * (long long)S;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  const bool has_hi = (t0 + 4) < S;
+  float4 c0 = ldg4(xr + t0);
+  float4 c1 = has_hi ? ldg4(xr + t0 + 4) : z4;
+  float4 p1 = (W > 1 && t0 >= 4) ? ldg4(xr + t0 - 4) : z4;
+  float4 p2 = (W > 5 && t0 >= 8) ? ldg4(xr + t0 - 8) : z4;
+
+  float v[16] = {p2.x, p2.y, p2.z, p2.w, p1.x, p1.y, p1.z, p1.w,
+                 c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  float wk[W];
+#pragma unroll
+  for (int k = 0; k < W; ++k) wk[k] = __ldg(w + (long long)d * W + k);
+  const float bd = __ldg(bias + d);
+
+  float o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float acc = bd;
+#pragma unroll
+    for (int k = 0; k < W; ++k) acc = fmaf(v[8 + j - (W - 1) + k], wk[k], acc);
+    o[j] = SILU ? silu_f(acc) : acc;
+  }
+  float* orow = out + row * (long long)S + t0;
+  *reinterpret_cast<float4*>(orow) = make_float4(o[0], o[1], o[2], o[3]);
+  if (has_hi) *reinterpret_cast<float4*>(orow + 4) = make_float4(o[4], o[5], o[6], o[7]);
+}
+
+// ---------------------------------------------------------------------------
+// BDS, fp32, any S / W / alignment: one output per thread.
+// ---------------------------------------------------------------------------
+template <bool SILU>
+__global__ void __launch_bounds__(256) conv_bds_scalar(const float* __restrict__ x, const float* __restrict__ w,
+                                                       const float* __restrict__ bias, float* __restrict__ out,
+                                                       int D, int S, int W, long long total) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const long long row = i / S;
+  const int t = (int)(i - row * S);
+  const int d = (int)(row % D);
+  const float* xr = x + row * (long long)S;
+  float acc = __ldg(bias + d);
+  for (int k = 0; k < W; ++k) {
+    const int ts = t - (W - 1) + k;
+    if (ts >= 0) acc = fmaf(__ldg(xr + ts), __ldg(w + (long long)d * W + k), acc);
+  }
+  out[i] = SILU ? silu_f(acc) : acc;
+}
+
+// ---------------------------------------------------------------------------
+// BSD (channel-last), fp32 or bf16, D % 8 == 0.
+// ---------------------------------------------------------------------------
+template <typename T>
+struct Vec8;
+template <>
+struct Vec8<__nv_bfloat16> {
+  uint4 raw;
+  __device__ __forceinline__ void load(const __nv_bfloat16* p) { raw = __ldg(reinterpret_cast<const uint4*>(p)); }
+  __device__ __forceinline__ void to_float(float* f) const {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 t = __bfloat1622float2(h[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+  __device__ __forceinline__ static void store(__nv_bfloat16* p, const float* f) {
+    uint4 r;
+    r.x = pack_bf16x2(f[0], f[1]);
+    r.y = pack_bf16x2(f[2], f[3]);
+    r.z = pack_bf16x2(f[4], f[5]);
+    r.w = pack_bf16x2(f[6], f[7]);
+    *reinterpret_cast<uint4*>(p) = r;
+  }
+};
+template <>
+struct Vec8<float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* p) {
+    a = ldg4(p);
+    b = ldg4(p + 4);
+  }
+  __device__ __forceinline__ void to_float(float* f) const {
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+  __device__ __forceinline__ static void store(float* p, const float* f) {
+    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(f[4], f[5], f[6], f[7]);
+  }
+};
+
+constexpr int kBsdThreads = 128;
+
+// GL = lanes per L2-norm group (G / 8), 0 = no norm. W taps are unrolled with
+// the W-1 previous rows kept in registers; other W go to conv_bsd_generic.
+template <typename T, int W, bool SILU, int GL, int TT>
+__global__ void __launch_bounds__(kBsdThreads) conv_bsd(const T* __restrict__ x, const float* __restrict__ w,
+                                                        const float* __restrict__ bias, T* __restrict__ out,
+                                                        int S, int D) {
+  const int c0 = (blockIdx.x * kBsdThreads + threadIdx.x) * 8;
+  const bool active = c0 < D;
+  const int cc = active ? c0 : 0;  // keep addresses valid for inactive lanes
+  const int t_begin = blockIdx.y * TT;
+  const long long bbase = (long long)blockIdx.z * S * D;
+  const T* xb = x + bbase + cc;
+  T* ob = out + bbase + cc;
+
+  float wr[8][W];
+  float bsv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    bsv[j] = __ldg(bias + cc + j);
+#pragma unroll
+    for (int k = 0; k < W; ++k) wr[j][k] = __ldg(w + (long long)(cc + j) * W + k);
+  }
+
+  // history: hist[k] = x row (t - (W-1) + k) for k < W-1
+  float hist[W > 1 ? W - 1 : 1][8];
+#pragma unroll
+  for (int k = 0; k < W - 1; ++k) {
+    const int ts = t_begin - (W - 1) + k;
+    if (ts >= 0 && active) {
+      Vec8<T> v;
+      v.load(xb + (long long)ts * D);
+      v.to_float(hist[k]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) hist[k][j] = 0.f;
+    }
+  }
+
+  // Issue all TT row loads first (independent), then compute.
+  Vec8<T> rows[TT];
+#pragma unroll
+  for (int i = 0; i < TT; ++i) {
+    const int t = t_begin + i;
+    if (t < S && active) rows[i].load(xb + (long long)t * D);
+  }
+
+#pragma unroll
+  for (int i = 0; i < TT; ++i) {
+    const int t = t_begin + i;
+    float cur[8];
+    rows[i].to_float(cur);
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float acc = bsv[j];
+#pragma unroll
+      for (int k = 0; k < W - 1; ++k) acc = fmaf(hist[k][j], wr[j][k], acc);
+      acc = fmaf(cur[j], wr[j][W - 1], acc);
+      o[j] = SILU ? silu_f(acc) : acc;
+    }
+#pragma unroll
+    for (int k = 0; k + 1 < W - 1; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) hist[k][j] = hist[k + 1][j];
+    if (W > 1) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) hist[W > 1 ? W - 2 : 0][j] = cur[j];
+    }
+    if (GL > 0) {
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(o[j], o[j], ss);
+#pragma unroll
+      for (int m = 1; m < GL; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+      const float r = rsqrtf(ss + 1e-6f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] *= r;
+    }
+    if (t < S && active) Vec8<T>::store(ob + (long long)t * D, o);
+  }
+}
+
+// Runtime-W channel-last fallback (W > 8): one thread = 8 channels x 1 step.
+template <typename T, bool SILU, int GL>
+__global__ void __launch_bounds__(kBsdThreads) conv_bsd_generic(const T* __restrict__ x,
+                                                                const float* __restrict__ w,
+                                                                const float* __restrict__ bias,
+                                                                T* __restrict__ out, int S, int D, int W) {
+  const int c0 = (blockIdx.x * kBsdThreads + threadIdx.x) * 8;
+  const bool active = c0 < D;
+  const int cc = active ? c0 : 0;
+  const int t = blockIdx.y;
+  const long long bbase = (long long)blockIdx.z * S * D;
+  float o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = __ldg(bias + cc + j);
+  for (int k = 0; k < W; ++k) {
+    const int ts = t - (W - 1) + k;
+    if (ts < 0 || !active) continue;
+    Vec8<T> v;
+    v.load(x + bbase + (long long)ts * D + cc);
+    float f[8];
+    v.to_float(f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = fmaf(f[j], __ldg(w + (long long)(cc + j) * W + k), o[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = SILU ? silu_f(o[j]) : o[j];
+  if (GL > 0) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(o[j], o[j], ss);
+#pragma unroll
+    for (int m = 1; m < GL; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    const float r = rsqrtf(ss + 1e-6f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] *= r;
+  }
+  if (active) Vec8<T>::store(out + bbase + (long long)t * D + cc, o);
+}
+
+// ---------------------------------------------------------------------------
+// dispatch
+// ---------------------------------------------------------------------------
+template <int W, bool SILU>
+void launch_bds_vec(const float* x, const float* w, const float* b, float* o, int B, int D, int S,
+                    cudaStream_t st) {
+  const int nseg_row = (S + 7) / 8;
+  const long long total = (long long)B * D * nseg_row;
+  const unsigned blocks = (unsigned)((total + 255) / 256);
+  conv_bds_vec8<W, SILU><<<blocks, 256, 0, st>>>(x, w, b, o, D, S, total, nseg_row);
+}
+
+template <bool SILU>
+int dispatch_bds(const float* x, const float* w, const float* b, float* o, int B, int D, int S, int W,
+                 cudaStream_t st) {
+  const bool vec = (S % 4 == 0) && W <= 8 && aligned16(x) && aligned16(o);
+  if (!vec) {
+    const long long total = (long long)B * D * S;
+    conv_bds_scalar<SILU><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(x, w, b, o, D, S, W, total);
+    return check_launch();
+  }
+  switch (W) {
+    case 1: launch_bds_vec<1, SILU>(x, w, b, o, B, D, S, st); break;
+    case 2: launch_bds_vec<2, SILU>(x, w, b, o, B, D, S, st); break;
+    case 3: launch_bds_vec<3, SILU>(x, w, b, o, B, D, S, st); break;
+    case 4: launch_bds_vec<4, SILU>(x, w, b, o, B, D, S, st); break;
+    case 5: launch_bds_vec<5, SILU>(x, w, b, o, B, D, S, st); break;
+    case 6: launch_bds_vec<6, SILU>(x, w, b, o, B, D, S, st); break;
+    case 7: launch_bds_vec<7, SILU>(x, w, b, o, B, D, S, st); break;
+    default: launch_bds_vec<8, SILU>(x, w, b, o, B, D, S, st); break;
+  }
+  return check_launch();
+}
+
+template <typename T, int W, bool SILU, int GL>
+void launch_bsd(const T* x, const float* w, const float* b, T* o, int B, int D, int S, cudaStream_t st) {
+  constexpr int TT = sizeof(T) == 2 ? 16 : 8;
+  dim3 grid((D / 8 + kBsdThreads - 1) / kBsdThreads, (S + TT - 1) / TT, B);
+  conv_bsd<T, W, SILU, GL, TT><<<grid, kBsdThreads, 0, st>>>(x, w, b, o, S, D);
+}
+
+template <typename T, bool SILU, int GL>
+int dispatch_bsd_w(const T* x, const float* w, const float* b, T* o, int B, int D, int S, int W,
+                   cudaStream_t st) {
+  switch (W) {
+    case 2: launch_bsd<T, 2, SILU, GL>(x, w, b, o, B, D, S, st); break;
+    case 3: launch_bsd<T, 3, SILU, GL>(x, w, b, o, B, D, S, st); break;
+    case 4: launch_bsd<T, 4, SILU, GL>(x, w, b, o, B, D, S, st); break;
+    default: {
+      dim3 grid((D / 8 + kBsdThreads - 1) / kBsdThreads, S, B);
+      conv_bsd_generic<T, SILU, GL><<<grid, kBsdThreads, 0, st>>>(x, w, b, o, S, D, W);
+    }
+  }
+  return check_launch();
+}
+
+template <typename T, bool SILU>
+int dispatch_bsd(const T* x, const float* w, const float* b, T* o, int B, int D, int S, int W, int G,
+                 cudaStream_t st) {
+  switch (G) {
+    case 0: return dispatch_bsd_w<T, SILU, 0>(x, w, b, o, B, D, S, W, st);
+    case 32: return dispatch_bsd_w<T, SILU, 4>(x, w, b, o, B, D, S, W, st);
+    case 64: return dispatch_bsd_w<T, SILU, 8>(x, w, b, o, B, D, S, W, st);
+    case 128: return dispatch_bsd_w<T, SILU, 16>(x, w, b, o, B, D, S, W, st);
+    case 256: return dispatch_bsd_w<T, SILU, 32>(x, w, b, o, B, D, S, W, st);
+    default: return THM_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace conv
+}  // namespace thm
+
+THM_STATUS_READER(thm_internal_status_conv, g_status_conv)
+
+extern "C" int thm_causal_conv1d_fwd(const void* x, const float* weight, const float* bias, void* out, int B,
+                                     int D, int S, int W, int layout, int dtype, int activation,
+                                     int l2norm_group, thm_stream_t stream) {
+  using namespace thm;
+  using namespace thm::conv;
+  if (B < 0 || D < 0 || S < 0 || W < 1) return THM_ERR_INVALID;
+  if (activation != THM_ACT_NONE && activation != THM_ACT_SILU) return THM_ERR_INVALID;
+  if (layout != THM_LAYOUT_BDS && layout != THM_LAYOUT_BSD) return THM_ERR_INVALID;
+  if (dtype != THM_F32 && dtype != THM_BF16) return THM_ERR_INVALID;
+  if ((long long)B * D * S == 0) return THM_OK;  // empty tensor: nothing to do
+  if (!x || !weight || !bias || !out) return THM_ERR_INVALID;
+  if (W > 64) return THM_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool silu = activation == THM_ACT_SILU;
+  if (layout == THM_LAYOUT_BDS) {
+    if (dtype != THM_F32 || l2norm_group != 0) return THM_ERR_UNSUPPORTED;
+    const float* xf = static_cast<const float*>(x);
+    float* of = static_cast<float*>(out);
+    return silu ? dispatch_bds<true>(xf, weight, bias, of, B, D, S, W, st)
+                : dispatch_bds<false>(xf, weight, bias, of, B, D, S, W, st);
+  }
+  if (D % 8 != 0) return THM_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(out)) return THM_ERR_ALIGNMENT;
+  if (l2norm_group != 0 && D % l2norm_group != 0) return THM_ERR_INVALID;
+  if (dtype == THM_BF16) {
+    auto xb = static_cast<const __nv_bfloat16*>(x);
+    auto ob = static_cast<__nv_bfloat16*>(out);
+    return silu ? dispatch_bsd<__nv_bfloat16, true>(xb, weight, bias, ob, B, D, S, W, l2norm_group, st)
+                : dispatch_bsd<__nv_bfloat16, false>(xb, weight, bias, ob, B, D, S, W, l2norm_group, st);
+  }
+  auto xf = static_cast<const float*>(x);
+  auto of = static_cast<float*>(out);
+  return silu ? dispatch_bsd<float, true>(xf, weight, bias, of, B, D, S, W, l2norm_group, st)
+              : dispatch_bsd<float, false>(xf, weight, bias, of, B, D, S, W, l2norm_group, st);
+}

@@ -1,0 +1,391 @@
+// chunk_fwd_o.cu -- gated-DeltaNet chunkwise output on tcgen05 tensor cores.
+//
+// Replaces kernels/chunk_fwd_o/kernel.py:52-136 (_chunk_fwd_o_kernel) and its
+// launcher :146-212. Per (b, h, chunk c, 64-wide V tile):
+//
+//   S = q k^T                                (M=64, N=64,  K=K)  tensor core
+//   G = q h[c]                               (M=64, N=VT,  K=K)  tensor core, tf32
+//   P = tril_{s<=t}(S * exp(g_t - g_s))      registers (TMEM -> regs -> smem)
+//   L = P v                                  (M=64, N=VT,  K=64) tensor core
+//   o = scale * (L + exp(g_t) * G)           registers (TMEM -> regs -> HBM)
+//
+// This equals the reference's scale*(tril((q e^g) k^T) (v e^-g) + (q e^g) h)
+// (kernels/chunk_fwd_o/reference.py:103-140); the decay is formed on the
+// masked 64x64 tile so no exp(-g) factor can overflow, and exp(g_t) is applied
+// to G's rows in the epilogue instead of to q.
+//
+// Data movement: q, k, v tiles and the fp32 state tile h[c][:, v-tile] arrive
+// by TMA on one mbarrier, already in UMMA canonical layouts: 128-B swizzle
+// (16-B chunks) for K-major and bf16 MN-major tiles, 128-B swizzle with 32-B
+// atoms for the MN-major tf32 tiles (h, and v when fp32); the
+// accumulators live in TMEM (G: VT columns, S then L: 64 columns). q·h runs
+// in kind::tf32 so h is consumed in fp32 straight from HBM; for bf16
+// activations q is widened to fp32 in shared memory first. For fp32
+// activations (the reference contract, fp32 throughout) S and L use 3xTF32
+// (x = hi + lo, hi = tf32(x): hi*hi + hi*lo + lo*hi), which keeps them at
+// fp32 accuracy; the lo tiles of q and k are reused for lo(P) once S is done.
+#include <cuda_bf16.h>
+
+#include "host_util.h"
+#include "sm100.cuh"
+
+THM_DEFINE_STATUS(g_status_o)
+
+namespace thm {
+namespace chunk_o {
+
+constexpr int kThreads = 128;
+constexpr int kBT = 64;  // chunk length
+constexpr int kVT = 64;  // V tile per CTA
+
+template <typename T, int K>
+struct Layout {
+  static constexpr int ES = sizeof(T);
+  static constexpr int Q_BYTES = kBT * K * ES;       // [64 x K]  K-major
+  static constexpr int V_BYTES = kBT * kVT * ES;     // [64 x VT] MN-major
+  static constexpr int H_BYTES = K * kVT * 4;        // [K x VT]  MN-major fp32
+  static constexpr int QG_BYTES = (ES == 2) ? kBT * K * 4 : 0;  // fp32 copy of q (bf16 path)
+  static constexpr int P_BYTES = kBT * kBT * ES;     // [64 x 64] K-major
+  static constexpr int LO_Q = (ES == 4) ? Q_BYTES : 0;  // fp32: lo(q), lo(k), then lo(P)
+  static constexpr int LO_V = (ES == 4) ? V_BYTES : 0;  // fp32: lo(v)
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + Q_BYTES;
+  static constexpr int OFF_H = OFF_V + V_BYTES;
+  static constexpr int OFF_QG = OFF_H + H_BYTES;
+  static constexpr int OFF_P = OFF_QG + QG_BYTES;
+  static constexpr int OFF_QLO = OFF_P + P_BYTES;
+  static constexpr int OFF_KLO = OFF_QLO + LO_Q;
+  static constexpr int OFF_VLO = OFF_KLO + LO_Q;
+  static constexpr int OFF_PLO = OFF_QLO;            // lo(P) reuses lo(q)
+  static constexpr int OFF_MISC = OFF_VLO + LO_V;    // g, exp(g), barriers, tmem slot
+  static constexpr int MISC_BYTES = 1024;
+  static constexpr int SMEM = OFF_MISC + MISC_BYTES + 1024;  // + alignment slack
+  static constexpr int TX_BYTES = 2 * Q_BYTES + V_BYTES + H_BYTES;
+  static constexpr uint32_t TMEM_COLS = 128;  // G [0,64) | S/L [64,128)
+};
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kThreads, 1)
+    chunk_fwd_o_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_h,
+                       const float* __restrict__ g, T* __restrict__ o, float scale, int T_len, int H, int V,
+                       int NT) {
+  using Ly = Layout<T, K>;
+  constexpr bool kBf16 = sizeof(T) == 2;
+  constexpr uint32_t kFmt = kBf16 ? 1u : 2u;       // UMMA A/B format of S and L
+  constexpr int kStep = kBf16 ? 16 : 8;            // K per MMA instruction
+  constexpr uint32_t kIdS = make_idesc(kFmt, 64, 64, 0, 0);
+  constexpr uint32_t kIdG = make_idesc(2u, 64, kVT, 0, 1);
+  constexpr uint32_t kIdL = make_idesc(kFmt, 64, kVT, 0, 1);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(sm);
+  float* sG = reinterpret_cast<float*>(sm + Ly::OFF_MISC);         // 64
+  float* sEG = sG + 64;                                             // 64
+  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(sm + Ly::OFF_MISC + 512);
+  uint64_t* bar_mma = bar_tma + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_tma + 2);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int vt = blockIdx.x;
+  const int c = blockIdx.y;
+  const int bh = blockIdx.z;
+  const int b = bh / H;
+  const int h = bh - b * H;
+  const int row0 = b * T_len + c * kBT;  // first (b, t) row of the chunk
+  const int v0 = vt * kVT;
+
+  if (tid == 0) {
+    mbar_init(bar_tma, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_h);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, Ly::TMEM_COLS);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t tG = tbase;       // columns [0, 64)
+  const uint32_t tS = tbase + 64;  // columns [64, 128): S, then L
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_tma, Ly::TX_BYTES);
+    constexpr int kBoxK = 128 / Ly::ES;  // elements per 128-B box row
+#pragma unroll
+    for (int j = 0; j < K / kBoxK; ++j) {
+      tma_load_3d(sm + Ly::OFF_Q + j * kBT * 128, &tm_q, bar_tma, j * kBoxK, h, row0);
+      tma_load_3d(sm + Ly::OFF_K + j * kBT * 128, &tm_k, bar_tma, j * kBoxK, h, row0);
+    }
+#pragma unroll
+    for (int j = 0; j < kVT / kBoxK; ++j)
+      tma_load_3d(sm + Ly::OFF_V + j * kBT * 128, &tm_v, bar_tma, v0 + j * kBoxK, h, row0);
+    const int hrow = ((b * NT + c) * H + h) * K;
+#pragma unroll
+    for (int j = 0; j < kVT / 32; ++j) tma_load_2d(sm + Ly::OFF_H + j * K * 128, &tm_h, bar_tma, v0 + j * 32, hrow);
+  }
+  if (tid < kBT) {
+    const float gv = g[(long long)(row0 + tid) * H + h];
+    sG[tid] = gv;
+    sEG[tid] = expf(gv);
+  }
+
+  bool ok = mbar_wait(bar_tma, 0, &g_status_o);
+  ok = __syncthreads_and(ok);
+  if (!ok) goto cleanup_tma;
+
+  if constexpr (!kBf16) {
+    split_tf32_tile(sm + Ly::OFF_Q, sm + Ly::OFF_QLO, Ly::Q_BYTES, tid, kThreads);
+    split_tf32_tile(sm + Ly::OFF_K, sm + Ly::OFF_KLO, Ly::Q_BYTES, tid, kThreads);
+    split_tf32_tile(sm + Ly::OFF_V, sm + Ly::OFF_VLO, Ly::V_BYTES, tid, kThreads);
+    fence_proxy_async_smem();
+    __syncthreads();
+  }
+  if constexpr (kBf16) {
+    // q (bf16, K-major SW128) -> fp32 copy (K-major SW128) for the tf32 q.h MMA.
+    const uint8_t* sq = sm + Ly::OFF_Q;
+    uint8_t* sqg = sm + Ly::OFF_QG;
+    for (int i = tid; i < kBT * K / 8; i += kThreads) {
+      const int t = i / (K / 8);
+      const int k0 = (i % (K / 8)) * 8;
+      const uint4 raw = *reinterpret_cast<const uint4*>(sq + sw128_offset(t, k0, kBT, 2));
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      float2 f0 = __bfloat1622float2(p2[0]), f1 = __bfloat1622float2(p2[1]);
+      float2 f2 = __bfloat1622float2(p2[2]), f3 = __bfloat1622float2(p2[3]);
+      *reinterpret_cast<float4*>(sqg + sw128_offset(t, k0, kBT, 4)) = make_float4(f0.x, f0.y, f1.x, f1.y);
+      *reinterpret_cast<float4*>(sqg + sw128_offset(t, k0 + 4, kBT, 4)) = make_float4(f2.x, f2.y, f3.x, f3.y);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+  }
+
+  if (tid == 0) {
+    tc_fence_after();
+    // S = q k^T
+#pragma unroll
+    for (int kk = 0; kk < K / kStep; ++kk) {
+      const uint32_t kb = kk * 32;  // bytes along K
+      const uint32_t off = (kb / 128) * (kBT * 128) + (kb % 128);
+      const uint64_t qd = make_sdesc(sbase + Ly::OFF_Q + off, 16, 1024);
+      const uint64_t kd = make_sdesc(sbase + Ly::OFF_K + off, 16, 1024);
+      mma_kind<kBf16>(tS, qd, kd, kIdS, kk > 0);
+      if constexpr (!kBf16) {
+        mma_tf32_ss(tS, qd, make_sdesc(sbase + Ly::OFF_KLO + off, 16, 1024), kIdS, 1);
+        mma_tf32_ss(tS, make_sdesc(sbase + Ly::OFF_QLO + off, 16, 1024), kd, kIdS, 1);
+      }
+    }
+    // G = q h  (tf32; A = q in fp32, B = h MN-major)
+    constexpr uint32_t kQgOff = kBf16 ? Ly::OFF_QG : Ly::OFF_Q;
+#pragma unroll
+    for (int kk = 0; kk < K / 8; ++kk) {
+      const uint32_t kb = kk * 32;
+      const uint32_t offa = (kb / 128) * (kBT * 128) + (kb % 128);
+      mma_tf32_ss(tG, make_sdesc(sbase + kQgOff + offa, 16, 1024),
+                  make_sdesc(sbase + Ly::OFF_H + kk * 8 * 128, K * 128, 512, kSw128Base32), kIdG, kk > 0);
+    }
+    mma_commit(bar_mma);
+  }
+
+  ok = mbar_wait(bar_mma, 0, &g_status_o);
+  ok = __syncthreads_and(ok);
+  if (!ok) goto cleanup_mma0;
+  tc_fence_after();
+
+  {
+    // P = tril(S * exp(g_t - g_s)) -> shared memory (A operand of P v).
+    const int t = warp * 16 + lane;  // valid for lane < 16
+    const uint32_t lane_addr = tS + ((uint32_t)(warp * 32) << 16);
+    float srow[64];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tmem_ld16(lane_addr + j * 16, srow + j * 16);
+    tmem_ld_wait();
+    if (lane < 16) {
+      const float gt = sG[t];
+      uint8_t* sp = sm + Ly::OFF_P;
+#pragma unroll
+      for (int s0 = 0; s0 < 64; s0 += 8) {
+        float pv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int s = s0 + j;
+          pv[j] = (s <= t) ? srow[s] * __expf(gt - sG[s]) : 0.0f;
+        }
+        if constexpr (kBf16) {
+          uint4 r;
+          r.x = pack_bf16x2(pv[0], pv[1]);
+          r.y = pack_bf16x2(pv[2], pv[3]);
+          r.z = pack_bf16x2(pv[4], pv[5]);
+          r.w = pack_bf16x2(pv[6], pv[7]);
+          *reinterpret_cast<uint4*>(sp + sw128_offset(t, s0, kBT, 2)) = r;
+        } else {
+          float hi[8], lo[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            hi[j] = tf32_round(pv[j]);
+            lo[j] = pv[j] - hi[j];
+          }
+          uint8_t* spl = sm + Ly::OFF_PLO;
+          *reinterpret_cast<float4*>(sp + sw128_offset(t, s0, kBT, 4)) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<float4*>(sp + sw128_offset(t, s0 + 4, kBT, 4)) = make_float4(hi[4], hi[5], hi[6], hi[7]);
+          *reinterpret_cast<float4*>(spl + sw128_offset(t, s0, kBT, 4)) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+          *reinterpret_cast<float4*>(spl + sw128_offset(t, s0 + 4, kBT, 4)) = make_float4(lo[4], lo[5], lo[6], lo[7]);
+        }
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+
+  if (tid == 0) {
+    tc_fence_after();
+    // L = P v (overwrites S's columns)
+#pragma unroll
+    for (int kk = 0; kk < kBT / kStep; ++kk) {
+      const uint32_t kb = kk * 32;
+      const uint32_t offa = (kb / 128) * (kBT * 128) + (kb % 128);
+      const uint64_t ad = make_sdesc(sbase + Ly::OFF_P + offa, 16, 1024);
+      if constexpr (kBf16) {
+        mma_bf16_ss(tS, ad, make_sdesc(sbase + Ly::OFF_V + kk * kStep * 128, kBT * 128, 1024, kSw128), kIdL, kk > 0);
+      } else {
+        const uint64_t vd = make_sdesc(sbase + Ly::OFF_V + kk * kStep * 128, kBT * 128, 512, kSw128Base32);
+        const uint64_t vl = make_sdesc(sbase + Ly::OFF_VLO + kk * kStep * 128, kBT * 128, 512, kSw128Base32);
+        mma_tf32_ss(tS, ad, vd, kIdL, kk > 0);
+        mma_tf32_ss(tS, ad, vl, kIdL, 1);
+        mma_tf32_ss(tS, make_sdesc(sbase + Ly::OFF_PLO + offa, 16, 1024), vd, kIdL, 1);
+      }
+    }
+    mma_commit(bar_mma);
+  }
+  ok = mbar_wait(bar_mma, 1, &g_status_o);
+  ok = __syncthreads_and(ok);
+  if (!ok) goto cleanup_mma1;
+  tc_fence_after();
+
+  {
+    // o = scale * (L + exp(g_t) G)
+    const int t = warp * 16 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const float eg = (lane < 16) ? sEG[t] * scale : 0.f;
+    T* orow = o + ((long long)(row0 + (lane < 16 ? t : 0)) * H + h) * V + v0;
+#pragma unroll
+    for (int j = 0; j < kVT / 16; ++j) {
+      float lv[16], gv[16];
+      tmem_ld16(tS + lane_off + j * 16, lv);
+      tmem_ld16(tG + lane_off + j * 16, gv);
+      tmem_ld_wait();
+      if (lane < 16) {
+        float r[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) r[i] = fmaf(lv[i], scale, gv[i] * eg);
+        if constexpr (kBf16) {
+          uint4 a, bq;
+          a.x = pack_bf16x2(r[0], r[1]);   a.y = pack_bf16x2(r[2], r[3]);
+          a.z = pack_bf16x2(r[4], r[5]);   a.w = pack_bf16x2(r[6], r[7]);
+          bq.x = pack_bf16x2(r[8], r[9]);  bq.y = pack_bf16x2(r[10], r[11]);
+          bq.z = pack_bf16x2(r[12], r[13]); bq.w = pack_bf16x2(r[14], r[15]);
+          *reinterpret_cast<uint4*>(orow + j * 16) = a;
+          *reinterpret_cast<uint4*>(orow + j * 16 + 8) = bq;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<float4*>(orow + j * 16 + i) = make_float4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, Ly::TMEM_COLS);
+  return;
+
+cleanup_mma1:
+  // An MMA wait ran out of time: give the in-flight MMAs one more bounded
+  // wait before releasing TMEM.
+  mbar_wait(bar_mma, 1, &g_status_o);
+  goto cleanup_tma;
+cleanup_mma0:
+  mbar_wait(bar_mma, 0, &g_status_o);
+cleanup_tma:
+  mbar_wait(bar_tma, 0, &g_status_o);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, Ly::TMEM_COLS);
+}
+
+template <typename T, int K>
+int launch(const void* q, const void* k, const void* v, const float* g, const float* hst, void* o, float scale,
+           int B, int T_len, int H, int V, cudaStream_t st) {
+  using Ly = Layout<T, K>;
+  const CUtensorMapDataType dt = sizeof(T) == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const int es = sizeof(T);
+  const int NT = T_len / kBT;
+  CUtensorMap tq, tk, tv, th;
+  const uint64_t rows = (uint64_t)B * T_len;
+  {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)H, rows};
+    uint64_t str[2] = {(uint64_t)K * es, (uint64_t)H * K * es};
+    uint32_t box[3] = {(uint32_t)(128 / es), 1u, (uint32_t)kBT};
+    int r = encode_tiled(&tq, dt, 3, q, dims, str, box);
+    if (r == THM_OK) r = encode_tiled(&tk, dt, 3, k, dims, str, box);
+    if (r != THM_OK) return r;
+  }
+  {
+    uint64_t dims[3] = {(uint64_t)V, (uint64_t)H, rows};
+    uint64_t str[2] = {(uint64_t)V * es, (uint64_t)H * V * es};
+    uint32_t box[3] = {(uint32_t)(128 / es), 1u, (uint32_t)kBT};
+    int r = encode_tiled(&tv, dt, 3, v, dims, str, box,
+                         es == 2 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    if (r != THM_OK) return r;
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)V, (uint64_t)B * NT * H * K};
+    uint64_t str[1] = {(uint64_t)V * 4};
+    uint32_t box[2] = {32u, (uint32_t)K};
+    int r = encode_tiled(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, hst, dims, str, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    if (r != THM_OK) return r;
+  }
+  auto kern = chunk_fwd_o_kernel<T, K>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
+    return THM_ERR_CUDA;
+  dim3 grid(V / kVT, NT, B * H);
+  kern<<<grid, kThreads, Ly::SMEM, st>>>(tq, tk, tv, th, g, static_cast<T*>(o), scale, T_len, H, V, NT);
+  return check_launch();
+}
+
+}  // namespace chunk_o
+}  // namespace thm
+
+THM_STATUS_READER(thm_internal_status_o, g_status_o)
+
+extern "C" int thm_chunk_fwd_o_fwd(const void* q, const void* k, const void* v, const float* g, const float* h,
+                                   void* o, float scale, int B, int T, int H, int K, int V, int dtype,
+                                   thm_stream_t stream) {
+  using namespace thm;
+  if (B < 0 || T < 0 || H < 0 || K <= 0 || V <= 0) return THM_ERR_INVALID;
+  if (T % 64 != 0) return THM_ERR_INVALID;
+  if (dtype != THM_F32 && dtype != THM_BF16) return THM_ERR_INVALID;
+  if ((long long)B * T * H == 0) return THM_OK;
+  if (!q || !k || !v || !g || !h || !o) return THM_ERR_INVALID;
+  if (!(K == 64 || K == 128) || V % 64 != 0 || V > 512) return THM_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(h) || !aligned16(o)) return THM_ERR_ALIGNMENT;
+  if ((long long)B * H > 65535 || T / 64 > 65535) return THM_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == THM_BF16) {
+    return K == 64 ? chunk_o::launch<__nv_bfloat16, 64>(q, k, v, g, h, o, scale, B, T, H, V, st)
+                   : chunk_o::launch<__nv_bfloat16, 128>(q, k, v, g, h, o, scale, B, T, H, V, st);
+  }
+  return K == 64 ? chunk_o::launch<float, 64>(q, k, v, g, h, o, scale, B, T, H, V, st)
+                 : chunk_o::launch<float, 128>(q, k, v, g, h, o, scale, B, T, H, V, st);
+}

@@ -1,0 +1,374 @@
+// sm100.cuh -- Blackwell (sm_100a) building blocks shared by the Theorem kernels.
+//
+// * mbarrier init / expect-tx / bounded wait (every wait has a time limit;
+//   a wait that runs out records THM_ERR_TIMEOUT in the translation unit's
+//   device status word and the caller unwinds instead of hanging the GPU);
+// * TMA tiled loads (cp.async.bulk.tensor, CTA-local destination, no
+//   multicast of any kind);
+// * tcgen05: TMEM alloc/dealloc, MMA issue (kind::f16 for bf16, kind::tf32
+//   for fp32 operands, fp32 accumulators), commit to an mbarrier, TMEM
+//   loads/stores for epilogues;
+// * UMMA shared-memory descriptors for the 128-byte-swizzled canonical
+//   layouts and the matching byte-offset function for tiles that threads
+//   write themselves.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/theorem_b200.h"
+
+namespace thm {
+
+// Per translation unit device status word (THM_OK or the first error code).
+// Each .cu that launches a kernel defines it through THM_DEFINE_STATUS().
+#define THM_DEFINE_STATUS(name)                                                  \
+  static __device__ unsigned int name = 0u;
+
+__device__ __forceinline__ void record_status(unsigned int* word, unsigned int code) {
+  atomicCAS(word, 0u, code);
+}
+
+// ---------------------------------------------------------------------------
+// time / addresses
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Longest any single wait may take before the kernel gives up (ns). The
+// kernels here finish in well under a millisecond per tile.
+constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete. Returns false (and
+// records THM_ERR_TIMEOUT) if it did not within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_status(status, THM_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// TMA (tiled tensor loads into this CTA's shared memory)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// Make generic-proxy writes to shared memory visible to the async proxy
+// (tensor core operand reads, TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05: tensor memory and MMA
+// ---------------------------------------------------------------------------
+// Executed by one full warp. Writes the TMEM base address to *dst.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] = (accumulate ? D : 0) + A[smem] * B[smem]
+__device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::f16 (bf16 operands) when BF16, else kind::tf32 (fp32 operands).
+template <bool BF16>
+__device__ __forceinline__ void mma_kind(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  if constexpr (BF16)
+    mma_bf16_ss(d_tmem, a_desc, b_desc, idesc, accumulate);
+  else
+    mma_tf32_ss(d_tmem, a_desc, b_desc, idesc, accumulate);
+}
+
+// Arrive on *bar once every tcgen05 op issued so far by this thread is done.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 bit, 16 consecutive columns per thread (lane i of the warp
+// reads TMEM lane (taddr.lane + i)). The tcgen05.wait::ld is issued inside the
+// same asm statement: the destination registers are undefined until the wait
+// completes, and a separate asm would let the compiler schedule their uses
+// above it.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 consecutive columns per thread, load and wait in one statement.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15,"
+      " %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32"
+      " [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// TMEM address of (lane, column) relative to an allocation base.
+__device__ __forceinline__ uint32_t tmem_addr(uint32_t base, uint32_t lane, uint32_t col) {
+  return base + (lane << 16) + col;
+}
+
+// ---------------------------------------------------------------------------
+// UMMA descriptors
+// ---------------------------------------------------------------------------
+// Instruction descriptor: fp32 accumulate, dense.
+//   ab_fmt: 1 = bf16 (kind::f16), 2 = tf32 (kind::tf32)
+//   a_mn / b_mn: operand is MN-major (1) or K-major (0)
+__host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_fmt, int M, int N, uint32_t a_mn, uint32_t b_mn) {
+  return (1u << 4)                       // D format F32
+         | (ab_fmt << 7) | (ab_fmt << 10)  // A, B formats
+         | (a_mn << 15) | (b_mn << 16)     // majors
+         | ((uint32_t)(N >> 3) << 17)      // N / 8
+         | ((uint32_t)(M >> 4) << 24);     // M / 16
+}
+
+// Shared-memory matrix descriptor for a 128-byte-swizzled canonical layout.
+//   layout 2 (SWIZZLE_128B, 16-B chunks, 8-row atoms):
+//     K-major : rows of 128 B, 8-row groups SBO (=1024) bytes apart; LBO unused.
+//     MN-major: 128-B rows along MN, 8 K-rows per 1024-B atom; K groups SBO
+//               bytes apart, MN blocks LBO bytes apart.
+//   layout 1 (SWIZZLE_128B_BASE32B, 32-B chunks, 4-row atoms): the only
+//     shared-memory layout tcgen05 accepts for MN-major tf32 operands; K
+//     groups of 4 rows SBO (=512) bytes apart, MN blocks LBO bytes apart.
+constexpr uint32_t kSw128 = 2u;
+constexpr uint32_t kSw128Base32 = 1u;
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                               uint32_t layout = kSw128) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version (sm100)
+  d |= (uint64_t)(layout & 7u) << 61;
+  return d;
+}
+
+// Byte offset of element (r, c) in a tile stored as 128-B-swizzled column
+// blocks: the tile's "row" index r selects a 128-B line, its "col" c indexes
+// within the row; columns are split into blocks of (128 / elem_bytes) and
+// each block is a contiguous [rows x 128 B] region. The 16-byte chunk index
+// inside a line is XORed with (r mod 8), matching TMA SWIZZLE_128B and the
+// UMMA canonical layouts (tile base 1024-B aligned).
+//   K-major operand : r = M/N row, c = K index
+//   MN-major operand: r = K index, c = M/N index
+__device__ __forceinline__ uint32_t sw128_offset(uint32_t r, uint32_t c, uint32_t rows, uint32_t elem_bytes) {
+  const uint32_t per_line = 128u / elem_bytes;
+  const uint32_t blk = c / per_line;
+  const uint32_t byte_in_line = (c % per_line) * elem_bytes;
+  const uint32_t chunk = (byte_in_line >> 4) ^ (r & 7u);
+  return blk * rows * 128u + r * 128u + (chunk << 4) + (byte_in_line & 15u);
+}
+
+// Same for the 32-byte-atom variant (layout 1, TMA SWIZZLE_128B_ATOM_32B):
+// the 32-B chunk index inside a line is XORed with (r mod 4).
+__device__ __forceinline__ uint32_t sw128b32_offset(uint32_t r, uint32_t c, uint32_t rows, uint32_t elem_bytes) {
+  const uint32_t per_line = 128u / elem_bytes;
+  const uint32_t blk = c / per_line;
+  const uint32_t byte_in_line = (c % per_line) * elem_bytes;
+  const uint32_t chunk = (byte_in_line >> 5) ^ (r & 3u);
+  return blk * rows * 128u + r * 128u + (chunk << 5) + (byte_in_line & 31u);
+}
+
+// ---------------------------------------------------------------------------
+// small helpers
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// Round an fp32 value to the nearest tf32 (low 13 mantissa bits cleared).
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// Split an fp32 tile in shared memory into hi = tf32(x) (in place) and
+// lo = x - hi (written at the same offset of `lo`), for 3xTF32 products
+// hi*hi + hi*lo + lo*hi. Elementwise, so it preserves any swizzle.
+__device__ __forceinline__ void split_tf32_tile(uint8_t* hi, uint8_t* lo, int bytes, int tid, int nthreads) {
+  for (int i = tid * 16; i < bytes; i += nthreads * 16) {
+    float4 x = *reinterpret_cast<float4*>(hi + i);
+    float4 h = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
+    *reinterpret_cast<float4*>(lo + i) = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+    *reinterpret_cast<float4*>(hi + i) = h;
+  }
+}
+
+// Scale every 128-B line of a [64-row x C-element] tile (stored as 128-B
+// column blocks of 64 lines each) by its row's factor. Swizzling permutes
+// 16/32-B chunks inside a line only, so a line belongs to one row.
+template <typename T>
+__device__ __forceinline__ void scale_rows(uint8_t* tile, int cols, const float* factor, int tid, int nthreads) {
+  const int chunks_per_line = 8;
+  const int lines = 64 * (cols * (int)sizeof(T) / 128);
+  for (int i = tid; i < lines * chunks_per_line; i += nthreads) {
+    const int line = i / chunks_per_line;
+    const int row = line % 64;
+    uint4* p = reinterpret_cast<uint4*>(tile + line * 128 + (i % chunks_per_line) * 16);
+    const float f = factor[row];
+    uint4 r = *p;
+    if constexpr (sizeof(T) == 2) {
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 x = __bfloat1622float2(h[j]);
+        h[j] = __floats2bfloat162_rn(x.x * f, x.y * f);
+      }
+    } else {
+      float* x = reinterpret_cast<float*>(&r);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) x[j] *= f;
+    }
+    *p = r;
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+
+}  // namespace thm

@@ -1,0 +1,146 @@
+"""Functional host API over the C ABI (torch tensors in, torch tensors out).
+
+Each function validates like the reference launcher it replaces (asserts on
+device, dtype, contiguity and shape), allocates its outputs with
+``torch.empty`` on the input's device, and launches on torch's current CUDA
+stream. Nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+BT = 64
+_ACT = {None: L.THM_ACT_NONE, "none": L.THM_ACT_NONE, "silu": L.THM_ACT_SILU}
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None:
+            assert t.is_cuda, "theorem_b200 ops need CUDA tensors (there is no CPU fallback)"
+
+
+def _contig(*ts):
+    for t in ts:
+        if t is not None:
+            assert t.is_contiguous(), "inputs must be contiguous"
+
+
+def causal_conv1d(x, weight, bias, activation=None, layout: str = "bds", l2norm_group: int = 0,
+                  out=None):
+    """Depthwise causal conv (kernels/causal_conv1d/kernel.py:170-230 contract).
+
+    layout "bds": x [B, D, S] fp32 (reference). layout "bsd": x [B, S, D] fp32 or
+    bf16 (channel-last chain). weight [D, W], bias [D] fp32. Optional SiLU and
+    per-``l2norm_group`` L2 norm (bsd only).
+    """
+    _cuda(x, weight, bias)
+    _contig(x, weight, bias)
+    assert weight.dtype == torch.float32 and bias.dtype == torch.float32, "weight/bias must be float32"
+    assert x.dim() == 3, "x must be rank 3"
+    if layout == "bds":
+        B, D, S = x.shape
+        lay = L.THM_LAYOUT_BDS
+    elif layout == "bsd":
+        B, S, D = x.shape
+        lay = L.THM_LAYOUT_BSD
+    else:
+        raise AssertionError(f"unknown layout {layout!r}")
+    Dw, W = weight.shape
+    assert D == Dw, f"channel mismatch: x has D={D}, weight has D={Dw}"
+    assert bias.shape == (D,), f"bias shape {tuple(bias.shape)} != ({D},)"
+    if out is None:
+        out = torch.empty_like(x)
+    st = L.stream_of(x)
+    L.check(L.load().thm_causal_conv1d_fwd(L.ptr(x), L.ptr(weight), L.ptr(bias), L.ptr(out), B, D, S, W,
+                                           lay, L.dtype_code(x), _ACT[activation], int(l2norm_group), st),
+            "thm_causal_conv1d_fwd")
+    return out
+
+
+def recompute_w_u(k, v, beta, A, g, a_mode: int = 0, w=None, u=None, A_out=None):
+    """w = A (k beta e^g), u = A (v beta) per 64-chunk (kernels/recompute_w_u/kernel.py:192-248).
+
+    a_mode 0 reads ``A`` [B,T,H,64] fp32; a_mode -1 / +1 computes
+    A = (I -/+ M)^-1 in-kernel (``A`` may be None; ``A_out`` receives it).
+    """
+    _cuda(k, v, beta, A, g)
+    _contig(k, v, beta, A, g)
+    B, T, H, K = k.shape
+    V = v.shape[-1]
+    assert v.shape == (B, T, H, V) and v.dtype == k.dtype
+    assert beta.shape == (B, T, H) and g.shape == (B, T, H)
+    assert beta.dtype == torch.float32 and g.dtype == torch.float32, "beta / g must be float32"
+    assert T % BT == 0, "T must be a multiple of BT (=64)"
+    if a_mode == 0:
+        assert A is not None and A.shape == (B, T, H, BT) and A.dtype == torch.float32
+    w = torch.empty_like(k) if w is None else w
+    u = torch.empty_like(v) if u is None else u
+    st = L.stream_of(k)
+    L.check(L.load().thm_recompute_w_u_fwd(L.ptr(k), L.ptr(v), L.ptr(beta), L.ptr(A) if a_mode == 0 else None,
+                                           L.ptr(g), L.ptr(w), L.ptr(u), L.ptr(A_out), B, T, H, K, V,
+                                           L.dtype_code(k), int(a_mode), st),
+            "thm_recompute_w_u_fwd")
+    return w, u
+
+
+def chunk_fwd_h(k, v, g, w=None, h0=None, mode: int = 0, want_v_new: bool = False,
+                want_final: bool = False, h=None, v_new=None):
+    """Inter-chunk state recurrence (kernels/chunk_fwd_h/kernel.py:141-191).
+
+    mode 0: reference recurrence, returns h [B,NT,H,K,V] of post-update states.
+    mode 1: gated delta rule (``v`` is u, ``w`` required), returns
+    (h of states entering each chunk, v_new or None, final or None).
+    """
+    _cuda(k, v, g, w, h0)
+    _contig(k, v, g, w, h0)
+    B, T, H, K = k.shape
+    V = v.shape[-1]
+    assert T % BT == 0, f"T={T} must be divisible by {BT}"
+    assert v.shape == (B, T, H, V) and v.dtype == k.dtype and g.shape == (B, T, H)
+    assert g.dtype == torch.float32
+    NT = T // BT
+    if h is None:
+        h = torch.empty(B, NT, H, K, V, device=k.device, dtype=torch.float32)
+    final = None
+    if mode == 1:
+        assert w is not None and w.shape == k.shape and w.dtype == k.dtype
+        if h0 is not None:
+            assert h0.shape == (B, H, K, V) and h0.dtype == torch.float32
+        if v_new is not None:
+            assert v_new.shape == v.shape and v_new.dtype == v.dtype and v_new.is_contiguous()
+        elif want_v_new:
+            v_new = torch.empty_like(v)
+        if want_final:
+            final = torch.empty(B, H, K, V, device=k.device, dtype=torch.float32)
+    else:
+        assert w is None and h0 is None and v_new is None
+    st = L.stream_of(k)
+    L.check(L.load().thm_chunk_fwd_h_fwd(L.ptr(k), L.ptr(w), L.ptr(v), L.ptr(g), L.ptr(h0), L.ptr(h),
+                                         L.ptr(v_new), L.ptr(final), B, T, H, K, V, L.dtype_code(k), int(mode),
+                                         st),
+            "thm_chunk_fwd_h_fwd")
+    if mode == 1:
+        return h, v_new, final
+    return h
+
+
+def chunk_fwd_o(q, k, v, g, h, scale: float, o=None):
+    """Chunkwise output (kernels/chunk_fwd_o/kernel.py:146-212)."""
+    _cuda(q, k, v, g, h)
+    _contig(q, k, v, g, h)
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    assert k.shape == q.shape and k.dtype == q.dtype and v.dtype == q.dtype
+    assert v.shape == (B, T, H, V) and g.shape == (B, T, H) and g.dtype == torch.float32
+    assert T % BT == 0, f"T={T} must be divisible by BT={BT}"
+    NT = T // BT
+    assert h.shape == (B, NT, H, K, V) and h.dtype == torch.float32, "h must be [B,NT,H,K,V] float32"
+    if o is None:
+        o = torch.empty(B, T, H, V, dtype=q.dtype, device=q.device)
+    st = L.stream_of(q)
+    L.check(L.load().thm_chunk_fwd_o_fwd(L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(h), L.ptr(o),
+                                         float(scale), B, T, H, K, V, L.dtype_code(q), st),
+            "thm_chunk_fwd_o_fwd")
+    return o
