@@ -1,0 +1,495 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 gated-DeltaNet forward hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (BASELINE.json metric "per-op us + %HBM / %TC peak; chained fwd
+tokens/s at 1/2/4/8 B200"): one step = one chained gated-DeltaNet layer
+forward at BASELINE config 5 (B=16, T=8192, H=16, K=V=128, D=2048, W=4, bf16)
+per GPU: causal_conv1d(+SiLU, +L2 norm) x3 -> recompute_w_u (in-kernel WY
+solve) -> chunk_fwd_h (delta rule) -> chunk_fwd_o. ``value`` = tokens/s over
+all ranks (each rank its own batch of 16 sequences: weak scaling, no
+collective on the data path), timed with CUDA events between a barrier +
+synchronize, max over ranks. Inputs are 1.6 GB per step per GPU (> L2), so no
+flush is needed between steps.
+
+Also on the line (rank 0, N=1 only): ``per_op`` (configs 1-4, L2 flushed
+between iterations), ``roofline`` of the dominant chain kernel measured live,
+``cpu_baseline`` (the reference's eager torch path restated in oracle/eager.py,
+fp32 on the host cores), ``e2e`` (the same step through the public API with
+pinned host buffers: H2D of inputs and D2H of o inside the timed region),
+``clocks`` sampled with nvidia-smi while the steps run, ``gpu_launches``.
+
+``--impl reference`` times the reference's CPU implementation (oracle/eager.py)
+on a bounded sample of the same workload (one sequence of the batch per step)
+on rank 0; other ranks exit.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CFG5 = dict(B=16, T=8192, H=16, K=128, V=128, W=4)
+METRIC = "chained_fwd_tokens_per_s"
+UNIT = "tokens/s"
+WORKLOAD = "BASELINE config 5: gated-DeltaNet layer fwd (conv+SiLU+L2norm -> recompute_w_u -> chunk_fwd_h -> chunk_fwd_o)"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return dict(hbm=float(d["hbm_gbs"]), tc=float(d["bf16_tflops"]), tc_sust=float(d["bf16_tflops_sustained"]),
+                    src="measured")
+    return dict(hbm=6650.0, tc=1590.0, tc_sust=1400.0, src="fallback")
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        import torch
+        pr = torch.cuda.get_device_properties(device_index)
+        self.bus = f"{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}".upper()
+        self.proc = None
+        self.lines: list[tuple[float, str]] = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+        time.sleep(0.5)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self, t0: float, t1: float):
+        if self.proc is None:
+            return None
+        time.sleep(0.3)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, pw, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        window = [l for ts, l in self.lines if t0 - 0.25 <= ts <= t1 + 0.25] or [l for _, l in self.lines]
+        for l in window:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 10 or self.bus not in f[1].upper():
+                continue
+            try:
+                sm.append(float(f[2]))
+                mx.append(float(f[3]))
+                pw.append(float(f[4]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[6:10]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "power_w_max": max(pw),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# synthetic inputs (BASELINE.json distributions; N(m, s2) = mean / variance)
+# ---------------------------------------------------------------------------
+def chain_inputs(B, T, H, K, V, W, seed, device, dtype):
+    import torch
+    import torch.nn.functional as F
+    g = torch.Generator(device=device).manual_seed(seed)
+    D, DV = H * K, H * V
+    xq = torch.randn(B, T, D, generator=g, device=device).to(dtype)
+    xk = torch.randn(B, T, D, generator=g, device=device).to(dtype)
+    xv = torch.randn(B, T, DV, generator=g, device=device).to(dtype)
+    cw = [torch.randn(n, W, generator=g, device=device) * 0.5 for n in (D, D, DV)]
+    cb = [torch.randn(n, generator=g, device=device) * math.sqrt(0.1) for n in (D, D, DV)]
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=g, device=device))
+    inc = F.logsigmoid(torch.randn(B, T, H, generator=g, device=device)) / 16
+    gate = inc.reshape(B, T // 64, 64, H).cumsum(2).reshape(B, T, H).contiguous()
+    return xq, xk, xv, cw, cb, beta, gate
+
+
+def chain_bytes(B, T, H, K, V, W):
+    """Algorithmic HBM bytes per launch of each chain kernel (bf16 activations)."""
+    rows = B * T * H
+    NT = T // 64
+    act_k, act_v = rows * K * 2, rows * V * 2
+    hbytes = B * NT * H * K * V * 4
+    return {
+        "causal_conv1d": 2 * act_k + H * K * (W + 1) * 4,          # one of q / k (v: same with V)
+        "recompute_w_u": 2 * act_k + 2 * act_v + 2 * rows * 4,      # k,v in; w,u out; beta,g
+        "chunk_fwd_h": 2 * act_k + act_v + rows * 4 + hbytes + act_v,  # k,w,u,g in; h, v_new out
+        "chunk_fwd_o": 2 * act_k + act_v + rows * 4 + hbytes + act_v,  # q,k,v_new,g,h in; o out
+    }
+
+
+# ---------------------------------------------------------------------------
+# the chained step on the GPU
+# ---------------------------------------------------------------------------
+def run_chain(args, rank, world, device):
+    import torch
+    import torch.distributed as dist
+    from theorem_b200 import _lib
+    from theorem_b200.chain import GatedDeltaNetForward
+
+    c = CFG5
+    B, T, H, K, V, W = c["B"], c["T"], c["H"], c["K"], c["V"], c["W"]
+    xq, xk, xv, cw, cb, beta, gate = chain_inputs(B, T, H, K, V, W, 1234 + rank, device, torch.bfloat16)
+    layer = GatedDeltaNetForward(H, K, V, cw, cb)
+    o = torch.empty(B, T, H, V, device=device, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream()
+
+    def step(evs=None):
+        if evs is None:
+            layer(xq, xk, xv, beta, gate, out=o, final_state=False)
+            return
+        # same calls as GatedDeltaNetForward.__call__, with events between kernels
+        from theorem_b200 import ops
+        bf = layer._buffers(xq, xv, B, T)
+        evs[0].record(stream)
+        ops.causal_conv1d(xq, layer.wq, layer.bq, "silu", "bsd", K, out=bf["q"].view(B, T, H * K))
+        ops.causal_conv1d(xk, layer.wk, layer.bk, "silu", "bsd", K, out=bf["k"].view(B, T, H * K))
+        ops.causal_conv1d(xv, layer.wv, layer.bv, "silu", "bsd", 0, out=bf["v"].view(B, T, H * V))
+        evs[1].record(stream)
+        w, u = ops.recompute_w_u(bf["k"], bf["v"], beta, None, gate, a_mode=1, w=bf["w"], u=bf["u"])
+        evs[2].record(stream)
+        h, vn, _ = ops.chunk_fwd_h(bf["k"], u, gate, w=w, mode=1, h=bf["h"], v_new=bf["v"])
+        evs[3].record(stream)
+        ops.chunk_fwd_o(bf["q"], bf["k"], vn, gate, h, layer.scale, o=o)
+        evs[4].record(stream)
+
+    sampler = ClockSampler(device.index) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    t_wall0 = time.time()
+    for i in range(args.steps):
+        step(evs[i])
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop(t_wall0, t_wall1) if sampler else None
+    ms = evs[0][0].elapsed_time(evs[-1][4])
+    per = {n: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
+           for j, n in enumerate(("causal_conv1d_x3", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"))}
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    status = _lib.device_status()
+    assert status == 0, f"in-kernel wait timed out (status {status})"
+    return dict(ms=ms, per_op_ms=per, clocks=clocks, tokens_per_rank=B * T, layer=layer,
+                inputs=(xq, xk, xv, beta, gate), out=o)
+
+
+def run_e2e(args, device, layer, inputs):
+    """Same step through the public API from pinned host memory, D2H of o included."""
+    import torch
+    xq, xk, xv, beta, gate = inputs
+    host = [t.cpu().pin_memory() for t in (xq, xk, xv, beta, gate)]
+    dev = [torch.empty_like(t) for t in (xq, xk, xv, beta, gate)]
+    B, T, H, V = xq.shape[0], xq.shape[1], layer.H, layer.V
+    o_host = torch.empty(B, T, H, V, dtype=xq.dtype).pin_memory()
+    o_dev = torch.empty(B, T, H, V, dtype=xq.dtype, device=device)
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    d2h = o_host.numel() * o_host.element_size()
+
+    def step():
+        for d_, h_ in zip(dev, host):
+            d_.copy_(h_, non_blocking=True)
+        layer(*dev, out=o_dev, final_state=False)
+        o_host.copy_(o_dev, non_blocking=True)
+
+    steps = max(2, min(args.steps, 10))
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"value": B * T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": steps,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": "theorem_b200.chain.GatedDeltaNetForward (C ABI) with pinned host buffers"}
+
+
+# ---------------------------------------------------------------------------
+# per-op configs 1-4 (rank 0, N=1)
+# ---------------------------------------------------------------------------
+def time_op(fn, iters=20, warm=3, flush=None):
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        ts.append(s.elapsed_time(e) * 1e3)
+    ts.sort()
+    return {"us_p50": ts[len(ts) // 2], "us_min": ts[0], "us_mean": sum(ts) / len(ts)}
+
+
+def per_op(device, pk):
+    import torch
+    import torch.nn.functional as F
+    from theorem_b200 import ops
+    out = {}
+    flush = torch.empty(512 * 1024 * 1024 // 4, device=device)  # 512 MB > 126 MB L2
+    g = torch.Generator(device=device).manual_seed(7)
+
+    def frac(bytes_, flops, us, tc_peak):
+        gbs = bytes_ / us / 1e3
+        tfl = flops / us / 1e6
+        return {"GB_s": gbs, "hbm_frac": gbs / pk["hbm"], "TFLOP_s": tfl, "tc_frac": tfl / tc_peak}
+
+    # config 1: causal_conv1d fp32 B1 D2560 S4096 W4 + SiLU (layout [B, D, S])
+    x = torch.randn(1, 2560, 4096, generator=g, device=device)
+    w = torch.randn(2560, 4, generator=g, device=device) * 0.5
+    b = torch.randn(2560, generator=g, device=device) * math.sqrt(0.1)
+    r = time_op(lambda: ops.causal_conv1d(x, w, b, activation="silu"), flush=flush)
+    by = 2 * x.numel() * 4 + 2560 * 5 * 4
+    r.update(frac(by, 2 * 4 * x.numel(), r["us_p50"], pk["tc"]), bytes=by, bound="hbm",
+             shape="B1 D2560 S4096 W4 fp32 +SiLU")
+    out["config1_causal_conv1d"] = r
+    del x
+
+    def dn(B, T, H, K, V, dtype=torch.bfloat16):
+        q = F.normalize(torch.randn(B, T, H, K, generator=g, device=device), dim=-1).to(dtype)
+        k = F.normalize(torch.randn(B, T, H, K, generator=g, device=device), dim=-1).to(dtype)
+        v = torch.randn(B, T, H, V, generator=g, device=device).to(dtype)
+        beta = torch.sigmoid(torch.randn(B, T, H, generator=g, device=device))
+        inc = F.logsigmoid(torch.randn(B, T, H, generator=g, device=device)) / 16
+        gate = inc.reshape(B, T // 64, 64, H).cumsum(2).reshape(B, T, H).contiguous()
+        return q, k, v, beta, gate
+
+    # config 2: recompute_w_u bf16, in-kernel A = (I + M)^-1, B2 T512 H3 K=V=64
+    B, T, H, K, V = 2, 512, 3, 64, 64
+    q, k, v, beta, gate = dn(B, T, H, K, V)
+    r = time_op(lambda: ops.recompute_w_u(k, v, beta, None, gate, a_mode=1), flush=flush)
+    nch = B * H * T // 64
+    fl = nch * (2 * 64 * 64 * K + 2 * 64 * 64 * (K + V) + 64 ** 3 // 3)
+    by = B * T * H * (2 * K * 2 + 2 * V * 2 + 8)
+    r.update(frac(by, fl, r["us_p50"], pk["tc"]), bytes=by, flops=fl, bound="latency (48 CTAs)",
+             shape="B2 T512 H3 K=V=64 bf16, fused A")
+    out["config2_recompute_w_u"] = r
+
+    # config 3: chunk_fwd_h delta rule bf16 / fp32 state, h0, B2 T1024 H3 K=V=64
+    B, T, H, K, V = 2, 1024, 3, 64, 64
+    q, k, v, beta, gate = dn(B, T, H, K, V)
+    w_, u_ = ops.recompute_w_u(k, v, beta, None, gate, a_mode=1)
+    h0 = torch.randn(B, H, K, V, generator=g, device=device) * math.sqrt(0.1)
+    hbuf = torch.empty(B, T // 64, H, K, V, device=device)
+    fin = torch.empty(B, H, K, V, device=device)
+
+    def h_call():
+        from theorem_b200 import _lib as L
+        L.check(L.load().thm_chunk_fwd_h_fwd(k.data_ptr(), w_.data_ptr(), u_.data_ptr(), gate.data_ptr(),
+                                             h0.data_ptr(), hbuf.data_ptr(), None, fin.data_ptr(), B, T, H, K, V,
+                                             L.THM_BF16, 1, torch.cuda.current_stream().cuda_stream), "h")
+    r = time_op(h_call, flush=flush)
+    fl = B * H * (T // 64) * (2 * 64 * K * V * 2)
+    by = B * T * H * (3 * K * 2 + 4) + hbuf.numel() * 4 + 2 * fin.numel() * 4
+    r.update(frac(by, fl, r["us_p50"], pk["tc"]), bytes=by, flops=fl, bound="serial latency (16 chunks x 6 CTAs)",
+             shape="B2 T1024 H3 K=V=64 bf16, delta rule, h0, final")
+    out["config3_chunk_fwd_h"] = r
+
+    # config 4: chunk_fwd_o bf16 B8 T4096 H16 K=V=128, h fp32
+    B, T, H, K, V = 8, 4096, 16, 128, 128
+    q, k, v, beta, gate = dn(B, T, H, K, V)
+    h = torch.randn(B, T // 64, H, K, V, generator=g, device=device) * 0.05
+    o = torch.empty(B, T, H, V, device=device, dtype=torch.bfloat16)
+    r = time_op(lambda: ops.chunk_fwd_o(q, k, v, gate, h, K ** -0.5, o=o), flush=flush)
+    fl = B * H * (T // 64) * (2 * 64 * 64 * K + 2 * 64 * 64 * V + 2 * 64 * K * V)
+    by = 3 * q.numel() * 2 + gate.numel() * 4 + h.numel() * 4 + o.numel() * 2
+    r.update(frac(by, fl, r["us_p50"], pk["tc"]), bytes=by, flops=fl, bound="hbm",
+             shape="B8 T4096 H16 K=V=128 bf16, h fp32")
+    out["config4_chunk_fwd_o"] = r
+    return out
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's eager torch path (oracle/eager.py), fp32
+# ---------------------------------------------------------------------------
+def cpu_chain_sample(seconds: float = 10.0, reps_min: int = 1, reps: int | None = None):
+    """Time the fp32 CPU chain on one sequence of config 5 (B=1, T=8192, H=16).
+    Returns (tokens/s, cores, seconds per sample, samples)."""
+    import torch
+    from oracle import eager
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    c = CFG5
+    T, H, K, V, W = c["T"], c["H"], c["K"], c["V"], c["W"]
+    xq, xk, xv, cw, cb, beta, gate = chain_inputs(1, T, H, K, V, W, 99, "cpu", torch.float32)
+    args = (xq, xk, xv, cw[0], cb[0], cw[1], cb[1], cw[2], cb[2], beta, gate, H, K, V)
+    times = []
+    t_start = time.time()
+    while True:
+        t0 = time.perf_counter()
+        eager.gated_delta_chain(*args)
+        times.append(time.perf_counter() - t0)
+        if reps is not None:
+            if len(times) >= reps:
+                break
+        elif len(times) >= reps_min and time.time() - t_start >= seconds:
+            break
+    per = statistics.mean(times)
+    return T / per, cores, per, len(times)
+
+
+def reference_arm(args, world, rank):
+    if rank != 0:
+        return 0
+    cores = os.cpu_count() or 1
+    log(f"[reference] fp32 CPU chain (oracle/eager.py) on {cores} cores, warmup {args.warmup}, steps {args.steps}")
+    cpu_chain_sample(reps=max(1, args.warmup))
+    v, cores, per, n = cpu_chain_sample(reps=max(1, args.steps))
+    c = CFG5
+    sample = (f"one sequence of config 5 per step (B=1 of 16, T=8192, all H=16 heads, K=V=128, D=2048, W=4), "
+              f"fp32 torch on CPU; tokens/s of that sample")
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, **c, "D": c["H"] * c["K"], "sample": "B=1 per step"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-per-op", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args(argv)
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return reference_arm(args, world, rank)
+
+    import torch
+    import torch.distributed as dist
+    assert torch.cuda.is_available(), "bench.py needs CUDA devices"
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    from theorem_b200 import _lib
+    _lib.load()
+
+    res = run_chain(args, rank, world, device)
+    pk = peaks()
+    extra = {}
+    if rank == 0 and world == 1:
+        if not args.no_e2e:
+            extra["e2e"] = run_e2e(args, device, res["layer"], res["inputs"])
+        if not args.no_per_op:
+            extra["per_op"] = per_op(device, pk)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    c = CFG5
+    B, T, H, K, V, W = c["B"], c["T"], c["H"], c["K"], c["V"], c["W"]
+    ms = res["ms"] / args.steps
+    value = world * res["tokens_per_rank"] / (ms / 1e3)
+    by = chain_bytes(B, T, H, K, V, W)
+    per_ms = res["per_op_ms"]
+    dom = max(("recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"), key=lambda n: per_ms[n])
+    if per_ms["causal_conv1d_x3"] / 3 > per_ms[dom]:
+        dom = "causal_conv1d"
+    dom_ms = per_ms["causal_conv1d_x3"] / 3 if dom == "causal_conv1d" else per_ms[dom]
+    achieved = by[dom] / (dom_ms * 1e-3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "dram_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(f"chain_{dom}")
+    chain_step_bytes = 2 * by["causal_conv1d"] + (2 * B * T * H * V * 2 + H * V * (W + 1) * 4) + \
+        by["recompute_w_u"] + by["chunk_fwd_h"] + by["chunk_fwd_o"]
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, **c, "D": H * K, "tokens_per_step_per_gpu": B * T,
+                   "parallelism": f"dp{world} (each rank its own B=16 batch; no collective on the data path)",
+                   "l2": "inputs 1.6 GB per step per GPU > 126 MB L2 (no flush needed)"},
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": pk["hbm"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm"], "traffic": traffic, "peak_source": pk["src"],
+                     "algorithmic_bytes_per_launch": by[dom], "avg_launch_ms": dom_ms},
+        "chain": {"per_op_ms": per_ms, "algorithmic_bytes_per_step": chain_step_bytes,
+                  "achieved_GB_s": chain_step_bytes / (ms * 1e-3) / 1e9},
+        "gpu_launches": 6 * args.steps,
+        "clocks": res["clocks"],
+    }
+    line.update(extra)
+    if not args.no_cpu and world == 1:
+        v, cores, per, n = cpu_chain_sample(seconds=10.0)
+        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": f"fp32 torch CPU chain (oracle/eager.py, restating the reference's "
+                                          f"eager baselines) on one sequence of config 5 (B=1, T=8192, H=16), "
+                                          f"{n} runs, {per:.2f} s each"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
