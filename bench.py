@@ -406,6 +406,31 @@ def reference_arm(args, world, rank):
 
 
 # ---------------------------------------------------------------------------
+def profile_op(args) -> int:
+    """Launch one op ``args.iters`` times on a small case (for ncu captures)."""
+    import torch
+    from theorem_b200 import ops
+    B, T, H, K, V = (int(x) for x in args.shape.split(","))
+    dev = torch.device("cuda", 0)
+    xq, xk, xv, cw, cb, beta, gate = chain_inputs(B, T, H, K, V, 4, 5, dev, torch.bfloat16)
+    q = ops.causal_conv1d(xq, cw[0], cb[0], "silu", "bsd", K).view(B, T, H, K)
+    k = ops.causal_conv1d(xk, cw[1], cb[1], "silu", "bsd", K).view(B, T, H, K)
+    v = ops.causal_conv1d(xv, cw[2], cb[2], "silu", "bsd", 0).view(B, T, H, V)
+    w, u = ops.recompute_w_u(k, v, beta, None, gate, a_mode=1)
+    h, vn, _ = ops.chunk_fwd_h(k, u, gate, w=w, mode=1, want_v_new=True)
+    fns = {
+        "causal_conv1d": lambda: ops.causal_conv1d(xq, cw[0], cb[0], "silu", "bsd", K),
+        "recompute_w_u": lambda: ops.recompute_w_u(k, v, beta, None, gate, a_mode=1, w=w, u=u),
+        "chunk_fwd_h": lambda: ops.chunk_fwd_h(k, u, gate, w=w, mode=1, h=h, v_new=vn),
+        "chunk_fwd_o": lambda: ops.chunk_fwd_o(q, k, vn, gate, h, K ** -0.5),
+    }
+    for _ in range(args.iters):
+        fns[args.op]()
+    torch.cuda.synchronize()
+    log(f"{args.op} x{args.iters} at B,T,H,K,V={args.shape}: ok")
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -415,7 +440,13 @@ def main(argv=None) -> int:
     ap.add_argument("--no-per-op", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--op", choices=["causal_conv1d", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"],
+                    help="profiling mode: launch one op (bf16, chain settings) --iters times and exit")
+    ap.add_argument("--shape", default="2,4096,16,128,128", help="B,T,H,K,V for --op")
+    ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args(argv)
+    if args.op:
+        return profile_op(args)
     args.warmup = max(3, args.warmup)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

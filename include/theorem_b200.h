@@ -47,10 +47,10 @@ typedef enum { THM_ACT_NONE = 0, THM_ACT_SILU = 1 } thm_activation;
  *
  * layout THM_LAYOUT_BDS: x, out [B, D, S] (the reference layout, fp32 only).
  * layout THM_LAYOUT_BSD: x, out [B, S, D] channel-last (fp32 or bf16), as the
- *   gated-DeltaNet chain produces them; D % 8 == 0.
+ *   gated-DeltaNet chain produces them; D % 4 == 0.
  * weight [D, W] and bias [D] are fp32. 1 <= W <= 64 (BDS: W <= 8, BSD:
  * W in {2,3,4} take the unrolled fast paths).
- * l2norm_group (BSD only): 0, or G in {32,64,128,256}: after the
+ * l2norm_group (BSD only): 0, or G in {16,32,64,128}: after the
  *   activation every run of G consecutive channels of a time step is scaled
  *   by 1/sqrt(sum of squares + 1e-6) (the chain's q/k L2 norm over a head).
  * ------------------------------------------------------------------------- */

@@ -88,7 +88,7 @@ def test_empty_batch():
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("W", [2, 3, 4, 6])
-@pytest.mark.parametrize("G", [0, 64, 128])
+@pytest.mark.parametrize("G", [0, 16, 64, 128])
 def test_channel_last_silu_l2norm(dtype, W, G):
     """Chain front-end: [B,S,D] conv + SiLU (+ per-head L2 norm) in fp32 / bf16."""
     from theorem_b200 import ops

@@ -8,12 +8,13 @@
 //   out[b,d,t] = act(bias[d] + sum_{k<W} weight[d,k] * x[b,d,t-W+1+k])
 //
 // BDS ([B,D,S], S contiguous, fp32): one thread = 8 consecutive outputs of a
-//   row, float4 loads/stores; the halo is the previous one or two float4 of
-//   the same row (L1 hits).
-// BSD ([B,S,D], D contiguous, fp32/bf16): one thread = 8 consecutive channels
-//   x TT consecutive time steps; 16-byte (bf16) or 2x16-byte (fp32) loads,
+//   row, float4 loads/stores; the halo comes from the neighbouring lane by
+//   warp shuffle (lane 0 reads it from memory).
+// BSD ([B,S,D], D contiguous, fp32/bf16): one thread = 4 consecutive channels
+//   x a 256-step time strip, software-pipelined in tiles of 8 rows; 8-byte
+//   (bf16) or 16-byte (fp32) loads (a warp covers 128 consecutive channels),
 //   the W-1 previous rows held in registers; optional SiLU and per-group L2
-//   norm (warp shuffles over G/8 lanes) fused into the store.
+//   norm (warp shuffles over G/4 lanes) fused into the store.
 #include <cuda_bf16.h>
 
 #include "host_util.h"
@@ -24,7 +25,9 @@ THM_DEFINE_STATUS(g_status_conv)
 namespace thm {
 namespace conv {
 
-__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+// x * sigmoid(x) with the fast exp / divide intrinsics (rel. error ~1e-6; the
+// quotient goes to 0 for x < -88 where exp(-x) overflows).
+__device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
@@ -36,9 +39,11 @@ __global__ void __launch_bounds__(256) conv_bds_vec8(const float* __restrict__ x
                                                      const float* __restrict__ bias, float* __restrict__ out,
                                                      int D, int S, long long nseg_total, int nseg_row) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= nseg_total) return;
-  const long long row = i / nseg_row;
-  const int seg = (int)(i - row * nseg_row);
+  const int lane = threadIdx.x & 31;
+  const bool valid = i < nseg_total;
+  const long long ii = valid ? i : nseg_total - 1;
+  const long long row = ii / nseg_row;
+  const int seg = (int)(ii - row * nseg_row);
   const int d = (int)(row % D);
   const int t0 = seg * 8;
   const float* xr = x + row * (long long)S;
@@ -47,11 +52,26 @@ __global__ void __launch_bounds__(256) conv_bds_vec8(const float* __restrict__ x
   const bool has_hi = (t0 + 4) < S;
   float4 c0 = ldg4(xr + t0);
   float4 c1 = has_hi ? ldg4(xr + t0 + 4) : z4;
-  float4 p1 = (W > 1 && t0 >= 4) ? ldg4(xr + t0 - 4) : z4;
-  float4 p2 = (W > 5 && t0 >= 8) ? ldg4(xr + t0 - 8) : z4;
+  // The W-1 values before t0 are the previous segment's outputs' inputs: take
+  // them from lane-1 when it holds the previous segment of the same row,
+  // else (lane 0) from memory, else (row start) zeros.
+  float pv[8] = {__shfl_up_sync(0xffffffffu, c0.x, 1), __shfl_up_sync(0xffffffffu, c0.y, 1),
+                 __shfl_up_sync(0xffffffffu, c0.z, 1), __shfl_up_sync(0xffffffffu, c0.w, 1),
+                 __shfl_up_sync(0xffffffffu, c1.x, 1), __shfl_up_sync(0xffffffffu, c1.y, 1),
+                 __shfl_up_sync(0xffffffffu, c1.z, 1), __shfl_up_sync(0xffffffffu, c1.w, 1)};
+  if (seg == 0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) pv[j] = 0.f;
+  } else if (lane == 0) {
+    const float4 p2 = (W > 5) ? ldg4(xr + t0 - 8) : z4;
+    const float4 p1 = ldg4(xr + t0 - 4);
+    pv[0] = p2.x; pv[1] = p2.y; pv[2] = p2.z; pv[3] = p2.w;
+    pv[4] = p1.x; pv[5] = p1.y; pv[6] = p1.z; pv[7] = p1.w;
+  }
+  if (!valid) return;
 
-  float v[16] = {p2.x, p2.y, p2.z, p2.w, p1.x, p1.y, p1.z, p1.w,
-                 c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  float v[16] = {pv[0], pv[1], pv[2], pv[3], pv[4], pv[5], pv[6], pv[7],
+                 c0.x,  c0.y,  c0.z,  c0.w,  c1.x,  c1.y,  c1.z,  c1.w};
   float wk[W];
 #pragma unroll
   for (int k = 0; k < W; ++k) wk[k] = __ldg(w + (long long)d * W + k);
@@ -92,105 +112,55 @@ __global__ void __launch_bounds__(256) conv_bds_scalar(const float* __restrict__
 }
 
 // ---------------------------------------------------------------------------
-// BSD (channel-last), fp32 or bf16, D % 8 == 0.
+// BSD (channel-last), fp32 or bf16, D % 4 == 0. One thread = 4 channels.
 // ---------------------------------------------------------------------------
 template <typename T>
-struct Vec8;
+struct Vec4;
 template <>
-struct Vec8<__nv_bfloat16> {
-  uint4 raw;
-  __device__ __forceinline__ void load(const __nv_bfloat16* p) { raw = __ldg(reinterpret_cast<const uint4*>(p)); }
+struct Vec4<__nv_bfloat16> {
+  uint2 raw;
+  __device__ __forceinline__ void load(const __nv_bfloat16* p) { raw = __ldg(reinterpret_cast<const uint2*>(p)); }
   __device__ __forceinline__ void to_float(float* f) const {
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float2 t = __bfloat1622float2(h[i]);
-      f[2 * i] = t.x;
-      f[2 * i + 1] = t.y;
-    }
+    float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
   }
   __device__ __forceinline__ static void store(__nv_bfloat16* p, const float* f) {
-    uint4 r;
+    uint2 r;
     r.x = pack_bf16x2(f[0], f[1]);
     r.y = pack_bf16x2(f[2], f[3]);
-    r.z = pack_bf16x2(f[4], f[5]);
-    r.w = pack_bf16x2(f[6], f[7]);
-    *reinterpret_cast<uint4*>(p) = r;
+    *reinterpret_cast<uint2*>(p) = r;
   }
 };
 template <>
-struct Vec8<float> {
-  float4 a, b;
-  __device__ __forceinline__ void load(const float* p) {
-    a = ldg4(p);
-    b = ldg4(p + 4);
-  }
-  __device__ __forceinline__ void to_float(float* f) const {
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-  }
+struct Vec4<float> {
+  float4 a;
+  __device__ __forceinline__ void load(const float* p) { a = ldg4(p); }
+  __device__ __forceinline__ void to_float(float* f) const { f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; }
   __device__ __forceinline__ static void store(float* p, const float* f) {
     *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
-    *reinterpret_cast<float4*>(p + 4) = make_float4(f[4], f[5], f[6], f[7]);
   }
 };
 
 constexpr int kBsdThreads = 128;
+constexpr int kBsdCh = 4;       // channels per thread
+constexpr int kBsdTile = 8;     // rows per pipelined tile
+constexpr int kBsdStrip = 256;  // time steps per thread strip
 
-// GL = lanes per L2-norm group (G / 8), 0 = no norm. W taps are unrolled with
-// the W-1 previous rows kept in registers; other W go to conv_bsd_generic.
-template <typename T, int W, bool SILU, int GL, int TT>
-__global__ void __launch_bounds__(kBsdThreads) conv_bsd(const T* __restrict__ x, const float* __restrict__ w,
-                                                        const float* __restrict__ bias, T* __restrict__ out,
-                                                        int S, int D) {
-  const int c0 = (blockIdx.x * kBsdThreads + threadIdx.x) * 8;
-  const bool active = c0 < D;
-  const int cc = active ? c0 : 0;  // keep addresses valid for inactive lanes
-  const int t_begin = blockIdx.y * TT;
-  const long long bbase = (long long)blockIdx.z * S * D;
-  const T* xb = x + bbase + cc;
-  T* ob = out + bbase + cc;
-
-  float wr[8][W];
-  float bsv[8];
+// One pipelined tile: rows t_first .. t_first+tt-1 from registers `rows`.
+// GL = lanes per L2-norm group (G / 4), 0 = no norm.
+template <typename T, int W, bool SILU, int GL>
+__device__ __forceinline__ void bsd_tile(Vec4<T>* rows, float (*hist)[kBsdCh], const float (*wr)[W],
+                                         const float* bsv, T* ob, int t_first, int S, int D, bool active, int tt) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    bsv[j] = __ldg(bias + cc + j);
-#pragma unroll
-    for (int k = 0; k < W; ++k) wr[j][k] = __ldg(w + (long long)(cc + j) * W + k);
-  }
-
-  // history: hist[k] = x row (t - (W-1) + k) for k < W-1
-  float hist[W > 1 ? W - 1 : 1][8];
-#pragma unroll
-  for (int k = 0; k < W - 1; ++k) {
-    const int ts = t_begin - (W - 1) + k;
-    if (ts >= 0 && active) {
-      Vec8<T> v;
-      v.load(xb + (long long)ts * D);
-      v.to_float(hist[k]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) hist[k][j] = 0.f;
-    }
-  }
-
-  // Issue all TT row loads first (independent), then compute.
-  Vec8<T> rows[TT];
-#pragma unroll
-  for (int i = 0; i < TT; ++i) {
-    const int t = t_begin + i;
-    if (t < S && active) rows[i].load(xb + (long long)t * D);
-  }
-
-#pragma unroll
-  for (int i = 0; i < TT; ++i) {
-    const int t = t_begin + i;
-    float cur[8];
+  for (int i = 0; i < kBsdTile; ++i) {
+    if (i >= tt) break;
+    const int t = t_first + i;
+    float cur[kBsdCh];
     rows[i].to_float(cur);
-    float o[8];
+    float o[kBsdCh];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < kBsdCh; ++j) {
       float acc = bsv[j];
 #pragma unroll
       for (int k = 0; k < W - 1; ++k) acc = fmaf(hist[k][j], wr[j][k], acc);
@@ -200,62 +170,123 @@ __global__ void __launch_bounds__(kBsdThreads) conv_bsd(const T* __restrict__ x,
 #pragma unroll
     for (int k = 0; k + 1 < W - 1; ++k)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) hist[k][j] = hist[k + 1][j];
+      for (int j = 0; j < kBsdCh; ++j) hist[k][j] = hist[k + 1][j];
     if (W > 1) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) hist[W > 1 ? W - 2 : 0][j] = cur[j];
+      for (int j = 0; j < kBsdCh; ++j) hist[W > 1 ? W - 2 : 0][j] = cur[j];
     }
     if (GL > 0) {
       float ss = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ss = fmaf(o[j], o[j], ss);
+      for (int j = 0; j < kBsdCh; ++j) ss = fmaf(o[j], o[j], ss);
 #pragma unroll
       for (int m = 1; m < GL; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
       const float r = rsqrtf(ss + 1e-6f);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] *= r;
+      for (int j = 0; j < kBsdCh; ++j) o[j] *= r;
     }
-    if (t < S && active) Vec8<T>::store(ob + (long long)t * D, o);
+    if (t < S && active) Vec4<T>::store(ob + (long long)t * D, o);
   }
 }
 
-// Runtime-W channel-last fallback (W > 8): one thread = 8 channels x 1 step.
+template <typename T>
+__device__ __forceinline__ void bsd_load_tile(Vec4<T>* rows, const T* xb, int t_first, int S, int D, bool active) {
+#pragma unroll
+  for (int i = 0; i < kBsdTile; ++i) {
+    const int t = t_first + i;
+    if (t < S && active) rows[i].load(xb + (long long)t * D);
+  }
+}
+
+// A thread owns 4 channels over a 256-step time strip: tile i+1's rows are
+// loaded while tile i is computed and stored, and the W-1 previous rows are
+// carried in registers (only the strip start re-reads a halo).
+template <typename T, int W, bool SILU, int GL>
+__global__ void __launch_bounds__(kBsdThreads, 4) conv_bsd(const T* __restrict__ x, const float* __restrict__ w,
+                                                           const float* __restrict__ bias, T* __restrict__ out,
+                                                           int S, int D) {
+  const int c0 = (blockIdx.x * kBsdThreads + threadIdx.x) * kBsdCh;
+  const bool active = c0 < D;
+  const int cc = active ? c0 : 0;  // keep addresses valid for inactive lanes
+  const int t_begin = blockIdx.y * kBsdStrip;
+  const int t_end = min(S, t_begin + kBsdStrip);
+  const long long bbase = (long long)blockIdx.z * S * D;
+  const T* xb = x + bbase + cc;
+  T* ob = out + bbase + cc;
+
+  float wr[kBsdCh][W];
+  float bsv[kBsdCh];
+#pragma unroll
+  for (int j = 0; j < kBsdCh; ++j) {
+    bsv[j] = __ldg(bias + cc + j);
+#pragma unroll
+    for (int k = 0; k < W; ++k) wr[j][k] = __ldg(w + (long long)(cc + j) * W + k);
+  }
+  float hist[W > 1 ? W - 1 : 1][kBsdCh];
+#pragma unroll
+  for (int k = 0; k < W - 1; ++k) {
+    const int ts = t_begin - (W - 1) + k;
+    if (ts >= 0 && active) {
+      Vec4<T> v;
+      v.load(xb + (long long)ts * D);
+      v.to_float(hist[k]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kBsdCh; ++j) hist[k][j] = 0.f;
+    }
+  }
+
+  Vec4<T> ra[kBsdTile], rb[kBsdTile];
+  bsd_load_tile<T>(ra, xb, t_begin, S, D, active);
+#pragma unroll 1
+  for (int t = t_begin; t < t_end; t += 2 * kBsdTile) {
+    if (t + kBsdTile < t_end) bsd_load_tile<T>(rb, xb, t + kBsdTile, S, D, active);
+    bsd_tile<T, W, SILU, GL>(ra, hist, wr, bsv, ob, t, S, D, active, min(kBsdTile, t_end - t));
+    if (t + kBsdTile < t_end) {
+      if (t + 2 * kBsdTile < t_end) bsd_load_tile<T>(ra, xb, t + 2 * kBsdTile, S, D, active);
+      bsd_tile<T, W, SILU, GL>(rb, hist, wr, bsv, ob, t + kBsdTile, S, D, active,
+                               min(kBsdTile, t_end - t - kBsdTile));
+    }
+  }
+}
+
+// Runtime-W channel-last fallback (W not in {2,3,4}): one thread = 4 channels x 1 step.
 template <typename T, bool SILU, int GL>
 __global__ void __launch_bounds__(kBsdThreads) conv_bsd_generic(const T* __restrict__ x,
                                                                 const float* __restrict__ w,
                                                                 const float* __restrict__ bias,
                                                                 T* __restrict__ out, int S, int D, int W) {
-  const int c0 = (blockIdx.x * kBsdThreads + threadIdx.x) * 8;
+  const int c0 = (blockIdx.x * kBsdThreads + threadIdx.x) * kBsdCh;
   const bool active = c0 < D;
   const int cc = active ? c0 : 0;
   const int t = blockIdx.y;
   const long long bbase = (long long)blockIdx.z * S * D;
-  float o[8];
+  float o[kBsdCh];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o[j] = __ldg(bias + cc + j);
+  for (int j = 0; j < kBsdCh; ++j) o[j] = __ldg(bias + cc + j);
   for (int k = 0; k < W; ++k) {
     const int ts = t - (W - 1) + k;
     if (ts < 0 || !active) continue;
-    Vec8<T> v;
+    Vec4<T> v;
     v.load(x + bbase + (long long)ts * D + cc);
-    float f[8];
+    float f[kBsdCh];
     v.to_float(f);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = fmaf(f[j], __ldg(w + (long long)(cc + j) * W + k), o[j]);
+    for (int j = 0; j < kBsdCh; ++j) o[j] = fmaf(f[j], __ldg(w + (long long)(cc + j) * W + k), o[j]);
   }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o[j] = SILU ? silu_f(o[j]) : o[j];
+  for (int j = 0; j < kBsdCh; ++j) o[j] = SILU ? silu_f(o[j]) : o[j];
   if (GL > 0) {
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ss = fmaf(o[j], o[j], ss);
+    for (int j = 0; j < kBsdCh; ++j) ss = fmaf(o[j], o[j], ss);
 #pragma unroll
     for (int m = 1; m < GL; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
     const float r = rsqrtf(ss + 1e-6f);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] *= r;
+    for (int j = 0; j < kBsdCh; ++j) o[j] *= r;
   }
-  if (active) Vec8<T>::store(out + bbase + (long long)t * D + cc, o);
+  if (active) Vec4<T>::store(out + bbase + (long long)t * D + cc, o);
 }
 
 // ---------------------------------------------------------------------------
@@ -294,9 +325,8 @@ int dispatch_bds(const float* x, const float* w, const float* b, float* o, int B
 
 template <typename T, int W, bool SILU, int GL>
 void launch_bsd(const T* x, const float* w, const float* b, T* o, int B, int D, int S, cudaStream_t st) {
-  constexpr int TT = sizeof(T) == 2 ? 16 : 8;
-  dim3 grid((D / 8 + kBsdThreads - 1) / kBsdThreads, (S + TT - 1) / TT, B);
-  conv_bsd<T, W, SILU, GL, TT><<<grid, kBsdThreads, 0, st>>>(x, w, b, o, S, D);
+  dim3 grid((D / kBsdCh + kBsdThreads - 1) / kBsdThreads, (S + kBsdStrip - 1) / kBsdStrip, B);
+  conv_bsd<T, W, SILU, GL><<<grid, kBsdThreads, 0, st>>>(x, w, b, o, S, D);
 }
 
 template <typename T, bool SILU, int GL>
@@ -307,7 +337,7 @@ int dispatch_bsd_w(const T* x, const float* w, const float* b, T* o, int B, int 
     case 3: launch_bsd<T, 3, SILU, GL>(x, w, b, o, B, D, S, st); break;
     case 4: launch_bsd<T, 4, SILU, GL>(x, w, b, o, B, D, S, st); break;
     default: {
-      dim3 grid((D / 8 + kBsdThreads - 1) / kBsdThreads, S, B);
+      dim3 grid((D / kBsdCh + kBsdThreads - 1) / kBsdThreads, S, B);
       conv_bsd_generic<T, SILU, GL><<<grid, kBsdThreads, 0, st>>>(x, w, b, o, S, D, W);
     }
   }
@@ -319,10 +349,10 @@ int dispatch_bsd(const T* x, const float* w, const float* b, T* o, int B, int D,
                  cudaStream_t st) {
   switch (G) {
     case 0: return dispatch_bsd_w<T, SILU, 0>(x, w, b, o, B, D, S, W, st);
-    case 32: return dispatch_bsd_w<T, SILU, 4>(x, w, b, o, B, D, S, W, st);
-    case 64: return dispatch_bsd_w<T, SILU, 8>(x, w, b, o, B, D, S, W, st);
-    case 128: return dispatch_bsd_w<T, SILU, 16>(x, w, b, o, B, D, S, W, st);
-    case 256: return dispatch_bsd_w<T, SILU, 32>(x, w, b, o, B, D, S, W, st);
+    case 16: return dispatch_bsd_w<T, SILU, 4>(x, w, b, o, B, D, S, W, st);
+    case 32: return dispatch_bsd_w<T, SILU, 8>(x, w, b, o, B, D, S, W, st);
+    case 64: return dispatch_bsd_w<T, SILU, 16>(x, w, b, o, B, D, S, W, st);
+    case 128: return dispatch_bsd_w<T, SILU, 32>(x, w, b, o, B, D, S, W, st);
     default: return THM_ERR_UNSUPPORTED;
   }
 }
@@ -353,7 +383,7 @@ extern "C" int thm_causal_conv1d_fwd(const void* x, const float* weight, const f
     return silu ? dispatch_bds<true>(xf, weight, bias, of, B, D, S, W, st)
                 : dispatch_bds<false>(xf, weight, bias, of, B, D, S, W, st);
   }
-  if (D % 8 != 0) return THM_ERR_UNSUPPORTED;
+  if (D % 4 != 0) return THM_ERR_UNSUPPORTED;
   if (!aligned16(x) || !aligned16(out)) return THM_ERR_ALIGNMENT;
   if (l2norm_group != 0 && D % l2norm_group != 0) return THM_ERR_INVALID;
   if (dtype == THM_BF16) {
