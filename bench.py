@@ -142,11 +142,12 @@ def chain_inputs(B, T, H, K, V, W, seed, device, dtype):
 
 
 def chain_bytes(B, T, H, K, V, W):
-    """Algorithmic HBM bytes per launch of each chain kernel (bf16 activations)."""
+    """Algorithmic HBM bytes per launch of each chain kernel (bf16 activations,
+    per-chunk states h stored in bf16 as the chain does)."""
     rows = B * T * H
     NT = T // 64
     act_k, act_v = rows * K * 2, rows * V * 2
-    hbytes = B * NT * H * K * V * 4
+    hbytes = B * NT * H * K * V * 2
     return {
         "causal_conv1d": 2 * act_k + H * K * (W + 1) * 4,          # one of q / k (v: same with V)
         "recompute_w_u": 2 * act_k + 2 * act_v + 2 * rows * 4,      # k,v in; w,u out; beta,g
@@ -334,7 +335,7 @@ def per_op(device, pk):
         from theorem_b200 import _lib as L
         L.check(L.load().thm_chunk_fwd_h_fwd(k.data_ptr(), w_.data_ptr(), u_.data_ptr(), gate.data_ptr(),
                                              h0.data_ptr(), hbuf.data_ptr(), None, fin.data_ptr(), B, T, H, K, V,
-                                             L.THM_BF16, 1, torch.cuda.current_stream().cuda_stream), "h")
+                                             L.THM_BF16, L.THM_F32, 1, torch.cuda.current_stream().cuda_stream), "h")
     r = time_op(h_call, flush=flush)
     fl = B * H * (T // 64) * (2 * 64 * K * V * 2)
     by = B * T * H * (3 * K * 2 + 4) + hbuf.numel() * 4 + 2 * fin.numel() * 4

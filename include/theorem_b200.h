@@ -92,12 +92,13 @@ int thm_recompute_w_u_fwd(const void* k, const void* v, const float* beta, const
  *   h[b,c,h] = h_c (state BEFORE chunk c); `v` is u; v_new (optional)
  *   [B,T,H,V] in `dtype`; final_state (optional) [B,H,K,V] fp32 = h_NT.
  * k, w [B,T,H,K], v [B,T,H,V] in `dtype`; g [B,T,H] fp32;
- * h [B,T/64,H,K,V] fp32; h0 [B,H,K,V] fp32.
- * T % 64 == 0; K in {64, 128}; V in {64, 128}.
+ * h [B,T/64,H,K,V] in `h_dtype` (THM_F32 as the reference, or THM_BF16: the
+ * state itself is always carried in fp32, only the stored copy is rounded);
+ * h0 [B,H,K,V] fp32. T % 64 == 0; K in {64, 128}; V in {64, 128}.
  * ------------------------------------------------------------------------- */
 int thm_chunk_fwd_h_fwd(const void* k, const void* w, const void* v, const float* g, const float* h0,
-                        float* h, void* v_new, float* final_state, int B, int T, int H, int K, int V,
-                        int dtype, int mode, thm_stream_t stream);
+                        void* h, void* v_new, float* final_state, int B, int T, int H, int K, int V,
+                        int dtype, int h_dtype, int mode, thm_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * chunk_fwd_o -- replaces kernels/chunk_fwd_o/kernel.py:146-212
@@ -105,11 +106,14 @@ int thm_chunk_fwd_h_fwd(const void* k, const void* w, const void* v, const float
  *
  *   o = scale * ( tril_{s<=t}((q k^T) * exp(g_t - g_s)) v + (q * exp(g)) h[c] )
  * q, k [B,T,H,K], v [B,T,H,V], o [B,T,H,V] in `dtype`; g [B,T,H] fp32;
- * h [B,T/64,H,K,V] fp32 (used as given for chunk c).
- * T % 64 == 0; K in {64, 128}; V % 64 == 0, V <= 512.
+ * h [B,T/64,H,K,V] in `h_dtype` (used as given for chunk c).
+ * T % 64 == 0; K in {64, 128}; V % 64 == 0, V <= 512 (h_dtype THM_BF16:
+ * dtype THM_BF16 and V in {64, 128}, run by a persistent warp-specialized
+ * kernel; h_dtype THM_F32: one CTA per (b, h, chunk, 64-wide V tile)).
  * ------------------------------------------------------------------------- */
-int thm_chunk_fwd_o_fwd(const void* q, const void* k, const void* v, const float* g, const float* h, void* o,
-                        float scale, int B, int T, int H, int K, int V, int dtype, thm_stream_t stream);
+int thm_chunk_fwd_o_fwd(const void* q, const void* k, const void* v, const float* g, const void* h, void* o,
+                        float scale, int B, int T, int H, int K, int V, int dtype, int h_dtype,
+                        thm_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Utilities

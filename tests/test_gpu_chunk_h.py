@@ -87,3 +87,19 @@ def test_delta_reduces_to_reference_recurrence():
     assert_close(hd[:, 1:].cpu(), href[:, :-1].cpu(), 1e-5, 1e-5, "shifted states")
     assert_close(fin.cpu(), href[:, -1].cpu(), 1e-5, 1e-5, "final")
     assert torch.equal(vn, v)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_bf16_state_output(mode):
+    """h stored in bf16 (the chain's layout) equals the fp32 h rounded to bf16."""
+    from theorem_b200 import ops
+    k, w, u, g, h0 = _delta_inputs(2, 512, 2, 128, 128, 31 + mode, torch.bfloat16)
+    args = dict(mode=mode)
+    if mode == 1:
+        args.update(w=w.to(DEV), h0=h0.to(DEV))
+    r32 = ops.chunk_fwd_h(k.to(DEV), u.to(DEV), g.to(DEV), **args)
+    r16 = ops.chunk_fwd_h(k.to(DEV), u.to(DEV), g.to(DEV), h_dtype=torch.bfloat16, **args)
+    h32 = r32[0] if mode == 1 else r32
+    h16 = r16[0] if mode == 1 else r16
+    assert h16.dtype == torch.bfloat16
+    assert torch.equal(h16, h32.to(torch.bfloat16))

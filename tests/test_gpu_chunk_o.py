@@ -80,3 +80,38 @@ def test_unsupported_head_dim_raises():
     with pytest.raises(AssertionError):
         ops.chunk_fwd_o(q, q, torch.zeros(1, 64, 1, 64, device=DEV), torch.zeros(1, 64, 1, device=DEV),
                         torch.zeros(1, 1, 1, 96, 64, device=DEV), 0.1)
+
+
+@pytest.mark.parametrize("K,V", [(64, 64), (64, 128), (128, 64), (128, 128)])
+def test_warp_specialized_bf16_state(K, V):
+    """bf16 q/k/v with a bf16 h: the persistent warp-specialized kernel."""
+    from theorem_b200 import ops
+    B, T, H = 2, 256, 3
+    d = deltanet_inputs(B, T, H, K, V, seed=11 * K + V)
+    gen = torch.Generator().manual_seed(3)
+    h = (torch.randn(B, T // 64, H, K, V, generator=gen) * 0.1).to(torch.bfloat16)
+    o = ops.chunk_fwd_o(d["q"].to(DEV), d["k"].to(DEV), d["v"].to(DEV), d["g"].to(DEV), h.to(DEV), K ** -0.5)
+    ref = orc.chunk_fwd_o(d["q"].float(), d["k"].float(), d["v"].float(), d["g"], h.float(), K ** -0.5)
+    assert o.dtype == torch.bfloat16
+    assert_close(o.float().cpu().double(), torch.from_numpy(ref), TOL, TOL, f"K={K} V={V}")
+
+
+def test_warp_specialized_many_units_per_cta():
+    """1024 (b, chunk, h) units over <= 148 persistent CTAs: every ring stage and
+    TMEM buffer is reused several times."""
+    from theorem_b200 import ops
+    B, T, H, K, V = 2, 4096, 8, 128, 128
+    d = deltanet_inputs(B, T, H, K, V, seed=21)
+    gen = torch.Generator().manual_seed(4)
+    h = (torch.randn(B, T // 64, H, K, V, generator=gen) * 0.05).to(torch.bfloat16)
+    o = ops.chunk_fwd_o(d["q"].to(DEV), d["k"].to(DEV), d["v"].to(DEV), d["g"].to(DEV), h.to(DEV), K ** -0.5)
+    oc = o.float().cpu()
+    assert torch.isfinite(oc).all()
+    for b, hh in [(0, 0), (1, 5), (1, 7)]:
+        sl = lambda t: t[b:b + 1, :, hh:hh + 1].float()
+        ref = orc.chunk_fwd_o(sl(d["q"]), sl(d["k"]), sl(d["v"]), sl(d["g"]), h[b:b + 1, :, hh:hh + 1].float(),
+                              K ** -0.5)
+        assert_close(oc[b:b + 1, :, hh:hh + 1].double(), torch.from_numpy(ref), TOL, TOL, f"b={b} h={hh}")
+    # repeated calls give identical results (no state leaks between launches)
+    o2 = ops.chunk_fwd_o(d["q"].to(DEV), d["k"].to(DEV), d["v"].to(DEV), d["g"].to(DEV), h.to(DEV), K ** -0.5)
+    assert torch.equal(o, o2)

@@ -14,8 +14,10 @@ behind a Mamba-2 causal conv. This module chains them the gated-DeltaNet way:
 
 Inputs xq, xk, xv are channel-last [B, T, H*K] (bf16 or fp32); beta and g
 [B, T, H] fp32 (g already the within-chunk cumulative gate). Intermediates
-(q, k, v, w, u, v_new in the input dtype; h fp32 [B, T/64, H, K, V]) are kept
-in buffers reused across calls with the same shape.
+(q, k, v, w, u, v_new in the input dtype; h [B, T/64, H, K, V] in bf16 for
+bf16 inputs -- the state is carried in fp32 inside chunk_fwd_h and only its
+stored per-chunk copy is rounded -- else fp32) are kept in buffers reused
+across calls with the same shape.
 """
 from __future__ import annotations
 
@@ -49,7 +51,8 @@ class GatedDeltaNetForward:
                 v=torch.empty(B, T, H, V, device=dev, dtype=dt),
                 w=torch.empty(B, T, H, K, device=dev, dtype=dt),
                 u=torch.empty(B, T, H, V, device=dev, dtype=dt),
-                h=torch.empty(B, T // 64, H, K, V, device=dev, dtype=torch.float32),
+                h=torch.empty(B, T // 64, H, K, V, device=dev,
+                              dtype=torch.bfloat16 if dt == torch.bfloat16 else torch.float32),
             )
         return self._buf
 

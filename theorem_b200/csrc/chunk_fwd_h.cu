@@ -49,11 +49,32 @@ struct Layout {
   static constexpr uint32_t TMEM_COLS = 128;  // U [0,64) | X [64,128)
 };
 
-template <typename T, int K, int MODE>
+// Store one 64-wide row of the state (fp32 registers) as fp32 or bf16.
+template <bool HB>
+__device__ __forceinline__ void store_state_row(void* dst, const float* S) {
+  if constexpr (HB) {
+    __nv_bfloat16* d = static_cast<__nv_bfloat16*>(dst);
+#pragma unroll
+    for (int j = 0; j < 64; j += 8) {
+      uint4 p;
+      p.x = pack_bf16x2(S[j], S[j + 1]);
+      p.y = pack_bf16x2(S[j + 2], S[j + 3]);
+      p.z = pack_bf16x2(S[j + 4], S[j + 5]);
+      p.w = pack_bf16x2(S[j + 6], S[j + 7]);
+      *reinterpret_cast<uint4*>(d + j) = p;
+    }
+  } else {
+    float* d = static_cast<float*>(dst);
+#pragma unroll
+    for (int j = 0; j < 64; j += 4) *reinterpret_cast<float4*>(d + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+  }
+}
+
+template <typename T, int K, int MODE, bool HB>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_fwd_h_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const __grid_constant__ CUtensorMap tm_w, const float* __restrict__ g,
-                       const float* __restrict__ h0, float* __restrict__ hout, T* __restrict__ v_new,
+                       const float* __restrict__ h0, void* __restrict__ hout, T* __restrict__ v_new,
                        float* __restrict__ final_state, int T_len, int H, int V) {
   using Ly = Layout<T, K, MODE>;
   constexpr bool kBf16 = Ly::BF16;
@@ -148,13 +169,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sv = sk + Ly::K_BYTES;                           // v / u tile
     const uint32_t sw = sv + Ly::V_BYTES;                           // w tile
     const float* gc = sG + st * 64;
-    float* hdst = hout + ((((long long)b * NT + c) * H + hh) * K + kk) * V + v0;
+    const long long hoff = ((((long long)b * NT + c) * H + hh) * K + kk) * V + v0;
+    void* hdst = HB ? static_cast<void*>(static_cast<__nv_bfloat16*>(hout) + hoff)
+                    : static_cast<void*>(static_cast<float*>(hout) + hoff);
 
     if constexpr (MODE == 1) {
       // h[c] = state entering chunk c; S -> smem as the B operand of X = w S.
       if (srow_ok) {
-#pragma unroll
-        for (int j = 0; j < kVT; j += 4) *reinterpret_cast<float4*>(hdst + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+        store_state_row<HB>(hdst, S);
         uint8_t* ss = sm + Ly::OFF_S;
         if constexpr (kBf16) {
 #pragma unroll
@@ -294,11 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (srow_ok) {
 #pragma unroll
         for (int j = 0; j < kVT; ++j) S[j] = fmaf(eg, S[j], ur[j]);
-        if constexpr (MODE == 0) {
-#pragma unroll
-          for (int j = 0; j < kVT; j += 4)
-            *reinterpret_cast<float4*>(hdst + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
-        }
+        if constexpr (MODE == 0) store_state_row<HB>(hdst, S);
       }
     }
     tc_fence_before();
@@ -319,8 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tmem_dealloc(tbase, Ly::TMEM_COLS);
 }
 
-template <typename T, int K, int MODE>
-int launch(const void* k, const void* w, const void* v, const float* g, const float* h0, float* h, void* v_new,
+template <typename T, int K, int MODE, bool HB>
+int launch(const void* k, const void* w, const void* v, const float* g, const float* h0, void* h, void* v_new,
            float* final_state, int B, int T_len, int H, int V, cudaStream_t st) {
   using Ly = Layout<T, K, MODE>;
   constexpr bool bf = Ly::BF16;
@@ -344,7 +362,7 @@ int launch(const void* k, const void* w, const void* v, const float* g, const fl
     int r = encode_tiled(&tv, dt, 3, v, dims, str, box, mn_sw);
     if (r != THM_OK) return r;
   }
-  auto kern = chunk_fwd_h_kernel<T, K, MODE>;
+  auto kern = chunk_fwd_h_kernel<T, K, MODE, HB>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
     return THM_ERR_CUDA;
   dim3 grid(V / kVT, B * H);
@@ -353,10 +371,13 @@ int launch(const void* k, const void* w, const void* v, const float* g, const fl
 }
 
 template <typename T, int MODE>
-int dispatch_k(const void* k, const void* w, const void* v, const float* g, const float* h0, float* h, void* vn,
-               float* fs, int B, int T_len, int H, int K, int V, cudaStream_t st) {
-  if (K == 64) return launch<T, 64, MODE>(k, w, v, g, h0, h, vn, fs, B, T_len, H, V, st);
-  return launch<T, 128, MODE>(k, w, v, g, h0, h, vn, fs, B, T_len, H, V, st);
+int dispatch_k(const void* k, const void* w, const void* v, const float* g, const float* h0, void* h, void* vn,
+               float* fs, int B, int T_len, int H, int K, int V, bool hb, cudaStream_t st) {
+  if (K == 64)
+    return hb ? launch<T, 64, MODE, true>(k, w, v, g, h0, h, vn, fs, B, T_len, H, V, st)
+              : launch<T, 64, MODE, false>(k, w, v, g, h0, h, vn, fs, B, T_len, H, V, st);
+  return hb ? launch<T, 128, MODE, true>(k, w, v, g, h0, h, vn, fs, B, T_len, H, V, st)
+            : launch<T, 128, MODE, false>(k, w, v, g, h0, h, vn, fs, B, T_len, H, V, st);
 }
 
 }  // namespace chunk_h
@@ -365,11 +386,12 @@ int dispatch_k(const void* k, const void* w, const void* v, const float* g, cons
 THM_STATUS_READER(thm_internal_status_h, g_status_h)
 
 extern "C" int thm_chunk_fwd_h_fwd(const void* k, const void* w, const void* v, const float* g, const float* h0,
-                                   float* h, void* v_new, float* final_state, int B, int T, int H, int K, int V,
-                                   int dtype, int mode, thm_stream_t stream) {
+                                   void* h, void* v_new, float* final_state, int B, int T, int H, int K, int V,
+                                   int dtype, int h_dtype, int mode, thm_stream_t stream) {
   using namespace thm;
   if (B < 0 || T < 0 || H < 0 || K <= 0 || V <= 0 || T % 64 != 0) return THM_ERR_INVALID;
   if (dtype != THM_F32 && dtype != THM_BF16) return THM_ERR_INVALID;
+  if (h_dtype != THM_F32 && h_dtype != THM_BF16) return THM_ERR_INVALID;
   if (mode != 0 && mode != 1) return THM_ERR_INVALID;
   if (mode == 0 && (w || h0 || v_new || final_state)) return THM_ERR_INVALID;
   if (mode == 1 && !w) return THM_ERR_INVALID;
@@ -391,10 +413,11 @@ extern "C" int thm_chunk_fwd_h_fwd(const void* k, const void* w, const void* v, 
     return THM_ERR_ALIGNMENT;
   if ((long long)B * H > 65535) return THM_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool hb = h_dtype == THM_BF16;
   if (dtype == THM_BF16) {
-    return mode == 0 ? chunk_h::dispatch_k<__nv_bfloat16, 0>(k, w, v, g, h0, h, v_new, final_state, B, T, H, K, V, st)
-                     : chunk_h::dispatch_k<__nv_bfloat16, 1>(k, w, v, g, h0, h, v_new, final_state, B, T, H, K, V, st);
+    return mode == 0 ? chunk_h::dispatch_k<__nv_bfloat16, 0>(k, w, v, g, h0, h, v_new, final_state, B, T, H, K, V, hb, st)
+                     : chunk_h::dispatch_k<__nv_bfloat16, 1>(k, w, v, g, h0, h, v_new, final_state, B, T, H, K, V, hb, st);
   }
-  return mode == 0 ? chunk_h::dispatch_k<float, 0>(k, w, v, g, h0, h, v_new, final_state, B, T, H, K, V, st)
-                   : chunk_h::dispatch_k<float, 1>(k, w, v, g, h0, h, v_new, final_state, B, T, H, K, V, st);
+  return mode == 0 ? chunk_h::dispatch_k<float, 0>(k, w, v, g, h0, h, v_new, final_state, B, T, H, K, V, hb, st)
+                   : chunk_h::dispatch_k<float, 1>(k, w, v, g, h0, h, v_new, final_state, B, T, H, K, V, hb, st);
 }

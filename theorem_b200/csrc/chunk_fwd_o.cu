@@ -364,28 +364,320 @@ int launch(const void* q, const void* k, const void* v, const float* g, const fl
   return check_launch();
 }
 
+
+// ===========================================================================
+// Persistent warp-specialized variant (bf16 q/k/v/o, bf16 h), the chain's
+// kernel. One CTA per SM walks units (b, c, h) with h fastest:
+//   warp 0     TMA producer: q, k, v, h tiles + gates into a 2-stage ring
+//   warp 1     tcgen05 issuer (one thread), one unit ahead of the math warps:
+//                S(i)  = q k^T            M=64,  N=64, K=K   -> TMEM S[i%2]
+//                G(i)^T = h^T q^T         M=V,   N=64, K=K   -> TMEM G[i%2]
+//                L(i-1)^T = v^T P^T       M=V,   N=64, K=64  -> TMEM L[(i-1)%2]
+//   warps 2-5  P(i) = tril(S * e^{g_t-g_s}) -> smem (all 32 lanes via the
+//              16x256b TMEM shape); epilogue o^T = scale (L^T + G^T e^{g_t})
+//              from TMEM, staged through smem and written by TMA store.
+// Transposing L and G puts V on the MMA's M (=128 rows, full rate) and lets
+// the MN-major v and h tiles feed the tensor core straight from TMA.
+// ===========================================================================
+namespace ws {
+
+constexpr int kThreads = 192;
+constexpr int kMath = 128;
+
+template <int K, int V>
+struct Layout {
+  static constexpr int Q_BYTES = 64 * K * 2;
+  static constexpr int V_BYTES = 64 * V * 2;
+  static constexpr int H_BYTES = K * V * 2;
+  static constexpr int STAGE = 2 * Q_BYTES + V_BYTES + H_BYTES;
+  static constexpr int OFF_Q = 0, OFF_K = Q_BYTES, OFF_V = 2 * Q_BYTES, OFF_H = 2 * Q_BYTES + V_BYTES;
+  static constexpr int P_BYTES = 64 * 64 * 2;
+  static constexpr int OFF_P = 2 * STAGE;
+  static constexpr int OFF_O = OFF_P + 2 * P_BYTES;
+  static constexpr int O_BYTES = 64 * V * 2;
+  static constexpr int OFF_G = OFF_O + O_BYTES;      // gates [2][64] f32
+  static constexpr int OFF_EG = OFF_G + 512;         // exp(g) [2][64] f32
+  static constexpr int OFF_BAR = OFF_EG + 512;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+};
+
+template <int K, int V>
+__global__ void __launch_bounds__(kThreads, 1)
+    chunk_fwd_o_ws_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_h,
+                          const __grid_constant__ CUtensorMap tm_o, const float* __restrict__ g, float scale,
+                          int T_len, int H, int NT, int nunits) {
+  using Ly = Layout<K, V>;
+  constexpr uint32_t kIdS = make_idesc(1u, 64, 64, 0, 0);
+  constexpr uint32_t kIdG = make_idesc(1u, V, 64, 1, 0);
+  constexpr uint32_t kIdL = make_idesc(1u, V, 64, 1, 0);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(sm);
+  float* sGate = reinterpret_cast<float*>(sm + Ly::OFF_G);
+  float* sEg = reinterpret_cast<float*>(sm + Ly::OFF_EG);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::OFF_BAR);
+  uint64_t* full = bars;        // [2] TMA stage loaded (+ gates written)
+  uint64_t* empty = bars + 2;   // [2] stage consumed by the tensor core
+  uint64_t* sfull = bars + 4;   // [2] S in TMEM
+  uint64_t* pfull = bars + 6;   // [2] P in smem
+  uint64_t* ofull = bars + 8;   // [2] L, G in TMEM
+  uint64_t* tfree = bars + 10;  // [2] TMEM buffer read out
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full[i], 33);
+      mbar_init(&empty[i], 1);
+      mbar_init(&sfull[i], 1);
+      mbar_init(&pfull[i], kMath);
+      mbar_init(&ofull[i], 1);
+      mbar_init(&tfree[i], kMath);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    int i = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++i) {
+      const int st = i & 1;
+      if (i >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&empty[st], ((i >> 1) & 1) ^ 1, &g_status_o));
+        if (!ok) break;
+      }
+      const int hh = u % H, bc = u / H, c = bc % NT, b = bc / NT;
+      const int row0 = b * T_len + c * 64;
+      float* gs = sGate + st * 64;
+      gs[lane] = g[(long long)(row0 + lane) * H + hh];
+      gs[lane + 32] = g[(long long)(row0 + lane + 32) * H + hh];
+      if (lane == 0) {
+        uint8_t* stg = sm + st * Ly::STAGE;
+        mbar_arrive_expect_tx(&full[st], Ly::STAGE);
+#pragma unroll
+        for (int j = 0; j < K / 64; ++j) {
+          tma_load_3d(stg + Ly::OFF_Q + j * 8192, &tm_q, &full[st], j * 64, hh, row0);
+          tma_load_3d(stg + Ly::OFF_K + j * 8192, &tm_k, &full[st], j * 64, hh, row0);
+        }
+        const int hrow = ((b * NT + c) * H + hh) * K;
+#pragma unroll
+        for (int j = 0; j < V / 64; ++j) {
+          tma_load_3d(stg + Ly::OFF_V + j * 8192, &tm_v, &full[st], j * 64, hh, row0);
+          tma_load_2d(stg + Ly::OFF_H + j * K * 128, &tm_h, &full[st], j * 64, hrow);
+        }
+      }
+      mbar_arrive(&full[st]);
+    }
+  } else if (warp == 1) {
+    // ---------------- tcgen05 issuer ----------------
+    if (lane == 0) {
+      int i = 0;
+      int u = blockIdx.x;
+      while (true) {
+        const bool has = u < nunits;
+        if (has) {
+          const int st = i & 1;
+          const uint32_t ph = (i >> 1) & 1;
+          if (!mbar_wait(&full[st], ph, &g_status_o)) { ok = false; break; }
+          if (i >= 2 && !mbar_wait(&tfree[st], ph ^ 1, &g_status_o)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t stg = sbase + st * Ly::STAGE;
+          const uint32_t tS = tbase + 256 * st, tG = tS + 128;
+#pragma unroll
+          for (int kk = 0; kk < K / 16; ++kk) {
+            const uint32_t off = (kk / 4) * 8192 + (kk % 4) * 32;
+            mma_bf16_ss(tS, make_sdesc(stg + Ly::OFF_Q + off, 16, 1024), make_sdesc(stg + Ly::OFF_K + off, 16, 1024),
+                        kIdS, kk > 0);
+          }
+          mma_commit(&sfull[st]);
+#pragma unroll
+          for (int kk = 0; kk < K / 16; ++kk) {
+            const uint32_t off = (kk / 4) * 8192 + (kk % 4) * 32;
+            mma_bf16_ss(tG, make_sdesc(stg + Ly::OFF_H + kk * 2048, K * 128, 1024),
+                        make_sdesc(stg + Ly::OFF_Q + off, 16, 1024), kIdG, kk > 0);
+          }
+        }
+        if (i >= 1) {
+          const int j = i - 1, sj = j & 1;
+          if (!mbar_wait(&pfull[sj], (j >> 1) & 1, &g_status_o)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t stg = sbase + sj * Ly::STAGE;
+          const uint32_t tL = tbase + 256 * sj + 64;
+          const uint32_t sp = sbase + Ly::OFF_P + sj * Ly::P_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16_ss(tL, make_sdesc(stg + Ly::OFF_V + kk * 2048, 8192, 1024), make_sdesc(sp + kk * 32, 16, 1024),
+                        kIdL, kk > 0);
+          mma_commit(&ofull[sj]);
+          mma_commit(&empty[sj]);
+        }
+        if (!has) break;
+        ++i;
+        u += gridDim.x;
+      }
+    }
+  } else {
+    // ---------------- math warps: P and epilogue ----------------
+    const int mt = tid - 64;
+    const int sp = warp & 3;  // TMEM subpartition this warp may access
+    const uint32_t lane_base = (uint32_t)(32 * sp) << 16;
+    int i = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++i) {
+      const int st = i & 1;
+      const uint32_t ph = (i >> 1) & 1;
+      const int hh = u % H, bc = u / H, c = bc % NT, b = bc / NT;
+      const int row0 = b * T_len + c * 64;
+      const float* gs = sGate + st * 64;
+      float* eg = sEg + st * 64;
+      ok = mbar_wait(&full[st], ph, &g_status_o) && mbar_wait(&sfull[st], ph, &g_status_o);
+      if (!named_bar_and(2, kMath, ok)) { ok = false; break; }
+      tc_fence_after();
+      {
+        float sv[32];
+        tmem_ld_16x256b_x8(tbase + 256 * st + lane_base, sv);
+        const int r0 = 16 * sp + (lane >> 2), r1 = r0 + 8;
+        const float g0 = gs[r0], g1 = gs[r1];
+        uint8_t* pbuf = sm + Ly::OFF_P + st * Ly::P_BYTES;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int cc = 8 * j + 2 * (lane & 3);
+          const float gc0 = gs[cc], gc1 = gs[cc + 1];
+          const float p00 = (cc <= r0) ? sv[4 * j] * __expf(g0 - gc0) : 0.f;
+          const float p01 = (cc + 1 <= r0) ? sv[4 * j + 1] * __expf(g0 - gc1) : 0.f;
+          const float p10 = (cc <= r1) ? sv[4 * j + 2] * __expf(g1 - gc0) : 0.f;
+          const float p11 = (cc + 1 <= r1) ? sv[4 * j + 3] * __expf(g1 - gc1) : 0.f;
+          *reinterpret_cast<uint32_t*>(pbuf + sw128_offset(r0, cc, 64, 2)) = pack_bf16x2(p00, p01);
+          *reinterpret_cast<uint32_t*>(pbuf + sw128_offset(r1, cc, 64, 2)) = pack_bf16x2(p10, p11);
+        }
+        if (mt < 64) eg[mt] = __expf(gs[mt]) * scale;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&pfull[st]);
+
+      ok = mbar_wait(&ofull[st], ph, &g_status_o);
+      if (!named_bar_and(2, kMath, ok)) { ok = false; break; }
+      tc_fence_after();
+      float lv[64], gv[64];
+      const uint32_t tL = tbase + 256 * st + 64 + lane_base, tG = tbase + 256 * st + 128 + lane_base;
+      tmem_ld32(tL, lv);
+      tmem_ld32(tL + 32, lv + 32);
+      tmem_ld32(tG, gv);
+      tmem_ld32(tG + 32, gv + 32);
+      tc_fence_before();
+      mbar_arrive(&tfree[st]);
+      if (mt == 0) bulk_wait_group_read0();  // previous o tile has left smem
+      named_bar_sync(1, kMath);
+      const bool vok = (V == 128) || lane < 16;
+      const int vv = (V == 128) ? 32 * sp + lane : 16 * sp + lane;
+      if (vok) {
+        uint8_t* ob = sm + Ly::OFF_O + (vv / 64) * 8192;
+#pragma unroll
+        for (int t = 0; t < 64; ++t) {
+          const float o = fmaf(lv[t], scale, gv[t] * eg[t]);
+          *reinterpret_cast<__nv_bfloat16*>(ob + sw128_offset(t, vv % 64, 64, 2)) = __float2bfloat16_rn(o);
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(1, kMath);
+      if (mt == 0) {
+#pragma unroll
+        for (int j = 0; j < V / 64; ++j) tma_store_3d(&tm_o, sm + Ly::OFF_O + j * 8192, j * 64, hh, row0);
+        bulk_commit_group();
+      }
+    }
+    if (mt == 0) bulk_wait_group0();
+  }
+
+  if (!ok) record_status(&g_status_o, THM_ERR_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 512);
+}
+
+template <int K, int V>
+int launch(const void* q, const void* k, const void* v, const float* g, const void* hst, void* o, float scale,
+           int B, int T_len, int H, cudaStream_t st) {
+  using Ly = Layout<K, V>;
+  const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int NT = T_len / 64;
+  const uint64_t rows = (uint64_t)B * T_len;
+  const uint32_t box[3] = {64u, 1u, 64u};
+  CUtensorMap tq, tk, tv, th, to;
+  {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)H, rows};
+    uint64_t str[2] = {(uint64_t)K * 2, (uint64_t)H * K * 2};
+    int r = encode_tiled(&tq, dt, 3, q, dims, str, box);
+    if (r == THM_OK) r = encode_tiled(&tk, dt, 3, k, dims, str, box);
+    if (r != THM_OK) return r;
+  }
+  {
+    uint64_t dims[3] = {(uint64_t)V, (uint64_t)H, rows};
+    uint64_t str[2] = {(uint64_t)V * 2, (uint64_t)H * V * 2};
+    int r = encode_tiled(&tv, dt, 3, v, dims, str, box);
+    if (r == THM_OK) r = encode_tiled(&to, dt, 3, o, dims, str, box);
+    if (r != THM_OK) return r;
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)V, (uint64_t)B * NT * H * K};
+    uint64_t str[1] = {(uint64_t)V * 2};
+    uint32_t hbox[2] = {64u, (uint32_t)K};
+    int r = encode_tiled(&th, dt, 2, hst, dims, str, hbox);
+    if (r != THM_OK) return r;
+  }
+  auto kern = chunk_fwd_o_ws_kernel<K, V>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
+    return THM_ERR_CUDA;
+  const int nunits = B * NT * H;
+  const int grid = nunits < sm_count() ? nunits : sm_count();
+  kern<<<grid, kThreads, Ly::SMEM, st>>>(tq, tk, tv, th, to, g, scale, T_len, H, NT, nunits);
+  return check_launch();
+}
+
+}  // namespace ws
 }  // namespace chunk_o
 }  // namespace thm
 
 THM_STATUS_READER(thm_internal_status_o, g_status_o)
 
-extern "C" int thm_chunk_fwd_o_fwd(const void* q, const void* k, const void* v, const float* g, const float* h,
-                                   void* o, float scale, int B, int T, int H, int K, int V, int dtype,
+extern "C" int thm_chunk_fwd_o_fwd(const void* q, const void* k, const void* v, const float* g, const void* h,
+                                   void* o, float scale, int B, int T, int H, int K, int V, int dtype, int h_dtype,
                                    thm_stream_t stream) {
   using namespace thm;
   if (B < 0 || T < 0 || H < 0 || K <= 0 || V <= 0) return THM_ERR_INVALID;
   if (T % 64 != 0) return THM_ERR_INVALID;
   if (dtype != THM_F32 && dtype != THM_BF16) return THM_ERR_INVALID;
+  if (h_dtype != THM_F32 && h_dtype != THM_BF16) return THM_ERR_INVALID;
   if ((long long)B * T * H == 0) return THM_OK;
   if (!q || !k || !v || !g || !h || !o) return THM_ERR_INVALID;
   if (!(K == 64 || K == 128) || V % 64 != 0 || V > 512) return THM_ERR_UNSUPPORTED;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(h) || !aligned16(o)) return THM_ERR_ALIGNMENT;
   if ((long long)B * H > 65535 || T / 64 > 65535) return THM_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == THM_BF16) {
-    return K == 64 ? chunk_o::launch<__nv_bfloat16, 64>(q, k, v, g, h, o, scale, B, T, H, V, st)
-                   : chunk_o::launch<__nv_bfloat16, 128>(q, k, v, g, h, o, scale, B, T, H, V, st);
+  if (h_dtype == THM_BF16) {
+    // bf16 state: the persistent warp-specialized kernel (bf16 activations).
+    if (dtype != THM_BF16 || !(V == 64 || V == 128)) return THM_ERR_UNSUPPORTED;
+    if (K == 64)
+      return V == 64 ? chunk_o::ws::launch<64, 64>(q, k, v, g, h, o, scale, B, T, H, st)
+                     : chunk_o::ws::launch<64, 128>(q, k, v, g, h, o, scale, B, T, H, st);
+    return V == 64 ? chunk_o::ws::launch<128, 64>(q, k, v, g, h, o, scale, B, T, H, st)
+                   : chunk_o::ws::launch<128, 128>(q, k, v, g, h, o, scale, B, T, H, st);
   }
-  return K == 64 ? chunk_o::launch<float, 64>(q, k, v, g, h, o, scale, B, T, H, V, st)
-                 : chunk_o::launch<float, 128>(q, k, v, g, h, o, scale, B, T, H, V, st);
+  const float* hf = static_cast<const float*>(h);
+  if (dtype == THM_BF16) {
+    return K == 64 ? chunk_o::launch<__nv_bfloat16, 64>(q, k, v, g, hf, o, scale, B, T, H, V, st)
+                   : chunk_o::launch<__nv_bfloat16, 128>(q, k, v, g, hf, o, scale, B, T, H, V, st);
+  }
+  return K == 64 ? chunk_o::launch<float, 64>(q, k, v, g, hf, o, scale, B, T, H, V, st)
+                 : chunk_o::launch<float, 128>(q, k, v, g, hf, o, scale, B, T, H, V, st);
 }

@@ -86,12 +86,14 @@ def recompute_w_u(k, v, beta, A, g, a_mode: int = 0, w=None, u=None, A_out=None)
 
 
 def chunk_fwd_h(k, v, g, w=None, h0=None, mode: int = 0, want_v_new: bool = False,
-                want_final: bool = False, h=None, v_new=None):
+                want_final: bool = False, h=None, v_new=None, h_dtype=torch.float32):
     """Inter-chunk state recurrence (kernels/chunk_fwd_h/kernel.py:141-191).
 
     mode 0: reference recurrence, returns h [B,NT,H,K,V] of post-update states.
     mode 1: gated delta rule (``v`` is u, ``w`` required), returns
     (h of states entering each chunk, v_new or None, final or None).
+    h is stored in ``h_dtype`` (float32, or bfloat16 for the chain); the state
+    itself is carried in fp32.
     """
     _cuda(k, v, g, w, h0)
     _contig(k, v, g, w, h0)
@@ -102,7 +104,8 @@ def chunk_fwd_h(k, v, g, w=None, h0=None, mode: int = 0, want_v_new: bool = Fals
     assert g.dtype == torch.float32
     NT = T // BT
     if h is None:
-        h = torch.empty(B, NT, H, K, V, device=k.device, dtype=torch.float32)
+        h = torch.empty(B, NT, H, K, V, device=k.device, dtype=h_dtype)
+    assert h.shape == (B, NT, H, K, V) and h.dtype in (torch.float32, torch.bfloat16) and h.is_contiguous()
     final = None
     if mode == 1:
         assert w is not None and w.shape == k.shape and w.dtype == k.dtype
@@ -118,8 +121,8 @@ def chunk_fwd_h(k, v, g, w=None, h0=None, mode: int = 0, want_v_new: bool = Fals
         assert w is None and h0 is None and v_new is None
     st = L.stream_of(k)
     L.check(L.load().thm_chunk_fwd_h_fwd(L.ptr(k), L.ptr(w), L.ptr(v), L.ptr(g), L.ptr(h0), L.ptr(h),
-                                         L.ptr(v_new), L.ptr(final), B, T, H, K, V, L.dtype_code(k), int(mode),
-                                         st),
+                                         L.ptr(v_new), L.ptr(final), B, T, H, K, V, L.dtype_code(k),
+                                         L.dtype_code(h), int(mode), st),
             "thm_chunk_fwd_h_fwd")
     if mode == 1:
         return h, v_new, final
@@ -136,11 +139,12 @@ def chunk_fwd_o(q, k, v, g, h, scale: float, o=None):
     assert v.shape == (B, T, H, V) and g.shape == (B, T, H) and g.dtype == torch.float32
     assert T % BT == 0, f"T={T} must be divisible by BT={BT}"
     NT = T // BT
-    assert h.shape == (B, NT, H, K, V) and h.dtype == torch.float32, "h must be [B,NT,H,K,V] float32"
+    assert h.shape == (B, NT, H, K, V) and h.dtype in (torch.float32, torch.bfloat16), \
+        "h must be [B,NT,H,K,V] float32 (or bfloat16 with bfloat16 q/k/v)"
     if o is None:
         o = torch.empty(B, T, H, V, dtype=q.dtype, device=q.device)
     st = L.stream_of(q)
     L.check(L.load().thm_chunk_fwd_o_fwd(L.ptr(q), L.ptr(k), L.ptr(v), L.ptr(g), L.ptr(h), L.ptr(o),
-                                         float(scale), B, T, H, K, V, L.dtype_code(q), st),
+                                         float(scale), B, T, H, K, V, L.dtype_code(q), L.dtype_code(h), st),
             "thm_chunk_fwd_o_fwd")
     return o
