@@ -90,3 +90,23 @@ def test_given_A_bf16_operands(K, V):
     rw, ru = orc.recompute_w_u(k.float(), v.float(), beta, A, g)
     assert_close(w.float().cpu().double(), torch.from_numpy(rw), TOL, TOL, "w")
     assert_close(u.float().cpu().double(), torch.from_numpy(ru), TOL, TOL, "u")
+
+
+@pytest.mark.parametrize("sign", [1, -1])
+def test_fused_many_units_per_cta(sign):
+    """2048 (b, chunk, h) units over <= 148 persistent CTAs (both math groups,
+    every ring stage and TMEM buffer reused many times); A_out checked too."""
+    from theorem_b200 import ops
+    B, T, H, K, V = 4, 2048, 16, 128, 128
+    k, v, beta, g = _baseline_case(B, T, H, K, V, 40 + sign, torch.bfloat16)
+    A_out = torch.empty(B, T, H, 64, device=DEV)
+    w, u = ops.recompute_w_u(k.to(DEV), v.to(DEV), beta.to(DEV), None, g.to(DEV), a_mode=sign, A_out=A_out)
+    w2, u2 = ops.recompute_w_u(k.to(DEV), v.to(DEV), beta.to(DEV), None, g.to(DEV), a_mode=sign)
+    assert torch.equal(w, w2) and torch.equal(u, u2)
+    for b, hh in [(0, 0), (2, 9), (3, 15)]:
+        sl = lambda t: t[b:b + 1, :, hh:hh + 1].float()
+        A = orc.build_A(sl(k), sl(beta), sl(g), sign)
+        rw, ru = orc.recompute_w_u(sl(k), sl(v), sl(beta), A, sl(g))
+        assert_close(A_out[b:b + 1, :, hh:hh + 1].cpu().double(), torch.from_numpy(A), 1e-3, 1e-4, "A")
+        assert_close(w[b:b + 1, :, hh:hh + 1].float().cpu().double(), torch.from_numpy(rw), TOL, TOL, "w")
+        assert_close(u[b:b + 1, :, hh:hh + 1].float().cpu().double(), torch.from_numpy(ru), TOL, TOL, "u")

@@ -370,14 +370,14 @@ int launch(const void* q, const void* k, const void* v, const float* g, const fl
 // kernel. One CTA per SM walks units (b, c, h) with h fastest:
 //   warp 0     TMA producer: q, k, v, h tiles + gates into a 2-stage ring
 //   warp 1     tcgen05 issuer (one thread), one unit ahead of the math warps:
-//                S(i)  = q k^T            M=64,  N=64, K=K   -> TMEM S[i%2]
-//                G(i)^T = h^T q^T         M=V,   N=64, K=K   -> TMEM G[i%2]
-//                L(i-1)^T = v^T P^T       M=V,   N=64, K=64  -> TMEM L[(i-1)%2]
-//   warps 2-5  P(i) = tril(S * e^{g_t-g_s}) -> smem (all 32 lanes via the
-//              16x256b TMEM shape); epilogue o^T = scale (L^T + G^T e^{g_t})
-//              from TMEM, staged through smem and written by TMA store.
-// Transposing L and G puts V on the MMA's M (=128 rows, full rate) and lets
-// the MN-major v and h tiles feed the tensor core straight from TMA.
+//                S(i)    = q k^T        M=64, N=64, K=K   -> TMEM S[i%2]
+//                G(i)    = q h          M=64, N=V,  K=K   -> TMEM [i%2], lane 16
+//                L(i-1)  = P v          M=64, N=V,  K=64  -> TMEM [(i-1)%2], lane 0
+//   warps 2-5  P(i) = tril(S * e^{g_t-g_s}) -> smem, and the epilogue
+//              o = scale (L + e^{g_t} G), both with all 32 lanes through the
+//              16x256b TMEM shape; o is staged in smem and written by TMA store.
+// L and G are two M=64 accumulators sharing TMEM columns at lane offsets 0 and
+// 16; the MN-major v and h tiles feed the tensor core straight from TMA.
 // ===========================================================================
 namespace ws {
 
@@ -409,8 +409,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                           int T_len, int H, int NT, int nunits) {
   using Ly = Layout<K, V>;
   constexpr uint32_t kIdS = make_idesc(1u, 64, 64, 0, 0);
-  constexpr uint32_t kIdG = make_idesc(1u, V, 64, 1, 0);
-  constexpr uint32_t kIdL = make_idesc(1u, V, 64, 1, 0);
+  constexpr uint32_t kIdG = make_idesc(1u, 64, V, 0, 1);
+  constexpr uint32_t kIdL = make_idesc(1u, 64, V, 0, 1);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -492,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (i >= 2 && !mbar_wait(&tfree[st], ph ^ 1, &g_status_o)) { ok = false; break; }
           tc_fence_after();
           const uint32_t stg = sbase + st * Ly::STAGE;
-          const uint32_t tS = tbase + 256 * st, tG = tS + 128;
+          const uint32_t tS = tbase + 256 * st, tG = tS + 64 + (16u << 16);
 #pragma unroll
           for (int kk = 0; kk < K / 16; ++kk) {
             const uint32_t off = (kk / 4) * 8192 + (kk % 4) * 32;
@@ -503,8 +503,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < K / 16; ++kk) {
             const uint32_t off = (kk / 4) * 8192 + (kk % 4) * 32;
-            mma_bf16_ss(tG, make_sdesc(stg + Ly::OFF_H + kk * 2048, K * 128, 1024),
-                        make_sdesc(stg + Ly::OFF_Q + off, 16, 1024), kIdG, kk > 0);
+            mma_bf16_ss(tG, make_sdesc(stg + Ly::OFF_Q + off, 16, 1024),
+                        make_sdesc(stg + Ly::OFF_H + kk * 2048, K * 128, 1024), kIdG, kk > 0);
           }
         }
         if (i >= 1) {
@@ -516,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sp = sbase + Ly::OFF_P + sj * Ly::P_BYTES;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_bf16_ss(tL, make_sdesc(stg + Ly::OFF_V + kk * 2048, 8192, 1024), make_sdesc(sp + kk * 32, 16, 1024),
+            mma_bf16_ss(tL, make_sdesc(sp + kk * 32, 16, 1024), make_sdesc(stg + Ly::OFF_V + kk * 2048, 8192, 1024),
                         kIdL, kk > 0);
           mma_commit(&ofull[sj]);
           mma_commit(&empty[sj]);
@@ -568,26 +568,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait(&ofull[st], ph, &g_status_o);
       if (!named_bar_and(2, kMath, ok)) { ok = false; break; }
       tc_fence_after();
-      float lv[64], gv[64];
-      const uint32_t tL = tbase + 256 * st + 64 + lane_base, tG = tbase + 256 * st + 128 + lane_base;
-      tmem_ld32(tL, lv);
-      tmem_ld32(tL + 32, lv + 32);
-      tmem_ld32(tG, gv);
-      tmem_ld32(tG + 32, gv + 32);
-      tc_fence_before();
-      mbar_arrive(&tfree[st]);
       if (mt == 0) bulk_wait_group_read0();  // previous o tile has left smem
       named_bar_sync(1, kMath);
-      const bool vok = (V == 128) || lane < 16;
-      const int vv = (V == 128) ? 32 * sp + lane : 16 * sp + lane;
-      if (vok) {
-        uint8_t* ob = sm + Ly::OFF_O + (vv / 64) * 8192;
+      {
+        // o = scale L + e^{g_t} scale G for rows r0, r0 + 8, packed bf16 pairs
+        const int r0 = 16 * sp + (lane >> 2), r1 = r0 + 8;
+        const float e0 = eg[r0], e1 = eg[r1];
+        const uint32_t swz = (uint32_t)((lane >> 2) & 7);
+        const uint32_t tL = tbase + 256 * st + 64 + lane_base;
 #pragma unroll
-        for (int t = 0; t < 64; ++t) {
-          const float o = fmaf(lv[t], scale, gv[t] * eg[t]);
-          *reinterpret_cast<__nv_bfloat16*>(ob + sw128_offset(t, vv % 64, 64, 2)) = __float2bfloat16_rn(o);
+        for (int half = 0; half < V / 64; ++half) {
+          float lv[32], gv[32];
+          tmem_ld_16x256b_x8(tL + 64 * half, lv);
+          tmem_ld_16x256b_x8(tL + (16u << 16) + 64 * half, gv);
+          uint8_t* box = sm + Ly::OFF_O + half * 8192;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t off = (((uint32_t)j ^ swz) << 4) + (uint32_t)(lane & 3) * 4;
+            *reinterpret_cast<uint32_t*>(box + r0 * 128 + off) =
+                pack_bf16x2(fmaf(lv[4 * j], scale, gv[4 * j] * e0), fmaf(lv[4 * j + 1], scale, gv[4 * j + 1] * e0));
+            *reinterpret_cast<uint32_t*>(box + r1 * 128 + off) =
+                pack_bf16x2(fmaf(lv[4 * j + 2], scale, gv[4 * j + 2] * e1), fmaf(lv[4 * j + 3], scale, gv[4 * j + 3] * e1));
+          }
         }
       }
+      tc_fence_before();
+      mbar_arrive(&tfree[st]);
       fence_proxy_async_smem();
       named_bar_sync(1, kMath);
       if (mt == 0) {

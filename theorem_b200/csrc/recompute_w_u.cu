@@ -371,6 +371,422 @@ int dispatch(const void* k, const void* v, const float* beta, const float* A, co
   return THM_ERR_UNSUPPORTED;
 }
 
+
+// ===========================================================================
+// Persistent warp-specialized variant: bf16 k/v/w/u, A formed in-kernel.
+// One CTA per SM walks units (b, c, h), h fastest.
+//   warp 0      TMA producer: k, v tiles + beta, g of a unit into a 3-stage ring
+//   warp 1      tcgen05 issuer: W(i), U(i) as soon as A(i) is ready, then
+//               KK^T(i+2) into the TMEM region unit i's M formation released:
+//                 KK^T                  (M=64, N=64, K=K)
+//                 W = (A diag(beta e^g)) k   (M=64, N=K, K=64)  TMEM lane 0
+//                 U = (A diag(beta)) v       (M=64, N=V, K=64)  TMEM lane 16
+//   warps 2-5 / 6-9  two math groups taking alternate units. Per unit i:
+//               M from KK^T (TMEM) -> A = (I + sign M)^-1 as a 2x2 block
+//               inverse (two 32x32 forward substitutions, then
+//               A10 = -sign A11 M10 A00) -> the two column-scaled bf16 copies
+//               of A as MMA operands; then the epilogue of the group's
+//               previous unit (i-2), whose products finished meanwhile:
+//               TMEM -> smem -> TMA store of w, u.
+// Folding beta e^g / beta into A's columns keeps k and v raw, so the same TMA
+// tiles feed KK^T (K-major) and the W/U products (MN-major B). W and U share
+// TMEM columns as two M=64 accumulators at lane offsets 0 and 16.
+// ===========================================================================
+namespace ws {
+
+constexpr int kThreads = 320;
+constexpr int kGroup = 128;
+constexpr int kStages = 3;
+
+template <int K, int V>
+struct Layout {
+  static constexpr int KB = 64 * K * 2, VB = 64 * V * 2;
+  static constexpr int STAGE = KB + VB;
+  static constexpr int OFF_STAGE = 0;                    // [3] k | v
+  static constexpr int OFF_GRP = kStages * STAGE;        // per math group:
+  static constexpr int G_M = 0;                          //   M / T fp32 [64][64]; w staging
+  static constexpr int G_A = 16384;                      //   A fp32 [64][64];     u staging
+  static constexpr int G_AW = 32768;                     //   A diag(beta e^g) bf16, K-major
+  static constexpr int G_AU = G_AW + 8192;               //   A diag(beta) bf16, K-major
+  static constexpr int GRP = G_AU + 8192;
+  static constexpr int OFF_SC = OFF_GRP + 2 * GRP;       // beta, g, beta*e^g [3][3][64] f32
+  static constexpr int OFF_BAR = OFF_SC + kStages * 3 * 64 * 4;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+};
+
+// W (lane 0) and U (lane 16) are M=64 accumulators interleaved in the same
+// TMEM columns; the 16x256b shape gives each thread rows r0 = 16 sp + lane/4
+// and r0 + 8 with column pairs, packed to bf16x2 in the row-major staging tiles.
+template <int N>
+__device__ __forceinline__ void stage_rows_16x256b(uint32_t taddr, uint8_t* stage, int sp, int lane) {
+  const int r0 = 16 * sp + (lane >> 2), r1 = r0 + 8;
+  const uint32_t sw = (uint32_t)((lane >> 2) & 7);
+#pragma unroll
+  for (int half = 0; half < N / 64; ++half) {
+    float v[32];
+    tmem_ld_16x256b_x8(taddr + 64 * half, v);
+    uint8_t* box = stage + half * 8192;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t off = (((uint32_t)j ^ sw) << 4) + (uint32_t)(lane & 3) * 4;
+      *reinterpret_cast<uint32_t*>(box + r0 * 128 + off) = pack_bf16x2(v[4 * j], v[4 * j + 1]);
+      *reinterpret_cast<uint32_t*>(box + r1 * 128 + off) = pack_bf16x2(v[4 * j + 2], v[4 * j + 3]);
+    }
+  }
+}
+
+template <int K, int V>
+__device__ __forceinline__ void wu_epilogue(uint8_t* gb, uint32_t tbase, int grp, int sp, int lane, int mt,
+                                            uint64_t* tfree_o, const CUtensorMap* tm_w, const CUtensorMap* tm_u,
+                                            int hh, int row0, uint32_t bar_sync) {
+  using Ly = Layout<K, V>;
+  const uint32_t tW = tbase + 256 * grp + 64 + ((uint32_t)(32 * sp) << 16);
+  uint8_t* ws_ = gb + Ly::G_M;
+  uint8_t* us_ = gb + Ly::G_A;
+  stage_rows_16x256b<K>(tW, ws_, sp, lane);
+  stage_rows_16x256b<V>(tW + (16u << 16), us_, sp, lane);
+  tc_fence_before();
+  mbar_arrive(&tfree_o[grp]);
+  fence_proxy_async_smem();
+  named_bar_sync(bar_sync, kGroup);
+  if (mt == 0) {
+#pragma unroll
+    for (int j = 0; j < K / 64; ++j) tma_store_3d(tm_w, ws_ + j * 8192, j * 64, hh, row0);
+#pragma unroll
+    for (int j = 0; j < V / 64; ++j) tma_store_3d(tm_u, us_ + j * 8192, j * 64, hh, row0);
+    bulk_commit_group();
+  }
+}
+
+template <int K, int V>
+__global__ void __launch_bounds__(kThreads, 1)
+    recompute_w_u_ws_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                            const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_u,
+                            const float* __restrict__ beta, const float* __restrict__ g,
+                            float* __restrict__ a_out, int T_len, int H, int NT, int nunits, float sgn) {
+  using Ly = Layout<K, V>;
+  constexpr uint32_t kIdKK = make_idesc(1u, 64, 64, 0, 0);
+  constexpr uint32_t kIdW = make_idesc(1u, 64, K, 0, 1);
+  constexpr uint32_t kIdU = make_idesc(1u, 64, V, 0, 1);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(sm);
+  float* sSc = reinterpret_cast<float*>(sm + Ly::OFF_SC);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::OFF_BAR);
+  uint64_t* full = bars;          // [3] stage loaded (+ beta, g)
+  uint64_t* empty = bars + 3;     // [3] stage consumed by the tensor core
+  uint64_t* kfull = bars + 6;     // [2] KK^T in TMEM (per group)
+  uint64_t* tfree_k = bars + 8;   // [2] KK^T region read out
+  uint64_t* afull = bars + 10;    // [2] A operands in smem
+  uint64_t* ofull = bars + 12;    // [2] W^T, U^T in TMEM
+  uint64_t* tfree_o = bars + 14;  // [2] W/U region read out
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // units of this CTA: u_i = blockIdx.x + i * gridDim.x, i < n_local
+  const int n_local = nunits > (int)blockIdx.x ? (nunits - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full[i], 33);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kfull[i], 1);
+      mbar_init(&tfree_k[i], kGroup);
+      mbar_init(&afull[i], kGroup);
+      mbar_init(&ofull[i], 1);
+      mbar_init(&tfree_o[i], kGroup);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    for (int i = 0; i < n_local; ++i) {
+      const int u = blockIdx.x + i * gridDim.x;
+      const int st = i % kStages;
+      if (i >= kStages) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&empty[st], ((i / kStages) & 1) ^ 1, &g_status_wu));
+        if (!ok) break;
+      }
+      const int hh = u % H, bc = u / H, c = bc % NT, b = bc / NT;
+      const int row0 = b * T_len + c * 64;
+      float* sc = sSc + st * 192;
+#pragma unroll
+      for (int r = lane; r < 64; r += 32) {
+        const long long gi = (long long)(row0 + r) * H + hh;
+        const float bv = beta[gi], gv = g[gi];
+        sc[r] = bv;
+        sc[64 + r] = gv;
+        sc[128 + r] = bv * __expf(gv);
+      }
+      if (lane == 0) {
+        uint8_t* stg = sm + Ly::OFF_STAGE + st * Ly::STAGE;
+        mbar_arrive_expect_tx(&full[st], Ly::STAGE);
+#pragma unroll
+        for (int j = 0; j < K / 64; ++j) tma_load_3d(stg + j * 8192, &tm_k, &full[st], j * 64, hh, row0);
+#pragma unroll
+        for (int j = 0; j < V / 64; ++j) tma_load_3d(stg + Ly::KB + j * 8192, &tm_v, &full[st], j * 64, hh, row0);
+      }
+      mbar_arrive(&full[st]);
+    }
+  } else if (warp == 1) {
+    // ---------------- tcgen05 issuer ----------------
+    if (lane == 0) {
+      auto issue_kk = [&](int i) -> bool {
+        const int st = i % kStages, gi = i & 1;
+        if (!mbar_wait(&full[st], (i / kStages) & 1, &g_status_wu)) return false;
+        if (i >= 2 && !mbar_wait(&tfree_k[gi], ((i >> 1) & 1) ^ 1, &g_status_wu)) return false;
+        tc_fence_after();
+        const uint32_t sk = sbase + Ly::OFF_STAGE + st * Ly::STAGE;
+#pragma unroll
+        for (int q = 0; q < K / 16; ++q) {
+          const uint64_t d = make_sdesc(sk + (q / 4) * 8192 + (q % 4) * 32, 16, 1024);
+          mma_bf16_ss(tbase + 256 * gi, d, d, kIdKK, q > 0);
+        }
+        mma_commit(&kfull[gi]);
+        return true;
+      };
+      for (int i = 0; i < 2 && i < n_local && ok; ++i) ok = issue_kk(i);
+      for (int i = 0; i < n_local && ok; ++i) {
+        const int st = i % kStages, gi = i & 1;
+        const uint32_t ph = (i >> 1) & 1;
+        if (!mbar_wait(&afull[gi], ph, &g_status_wu)) { ok = false; break; }
+        if (i >= 2 && !mbar_wait(&tfree_o[gi], ph ^ 1, &g_status_wu)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sk = sbase + Ly::OFF_STAGE + st * Ly::STAGE;
+        const uint32_t sv = sk + Ly::KB;
+        const uint32_t grp = sbase + Ly::OFF_GRP + gi * Ly::GRP;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint64_t aw = make_sdesc(grp + Ly::G_AW + q * 32, 16, 1024);
+          const uint64_t au = make_sdesc(grp + Ly::G_AU + q * 32, 16, 1024);
+          // W = A_w k at TMEM lane 0, U = A_u v at lane 16 (interleaved M=64 accumulators)
+          mma_bf16_ss(tbase + 256 * gi + 64, aw, make_sdesc(sk + q * 2048, 8192, 1024), kIdW, q > 0);
+          mma_bf16_ss(tbase + 256 * gi + 64 + (16u << 16), au, make_sdesc(sv + q * 2048, 8192, 1024), kIdU, q > 0);
+        }
+        mma_commit(&ofull[gi]);
+        mma_commit(&empty[st]);
+        if (i + 2 < n_local && !issue_kk(i + 2)) { ok = false; break; }
+      }
+    }
+  } else {
+    // ---------------- math groups ----------------
+    const int grp = (warp - 2) >> 2;  // 0: warps 2-5, 1: warps 6-9
+    const int mt = tid - 64 - grp * kGroup;
+    const int sp = warp & 3;          // TMEM subpartition of this warp
+    const uint32_t lane_base = (uint32_t)(32 * sp) << 16;
+    const uint32_t bar_sync = 1 + grp, bar_vote = 3 + grp;
+    uint8_t* gb = sm + Ly::OFF_GRP + grp * Ly::GRP;
+    float(*sM)[64] = reinterpret_cast<float(*)[64]>(gb + Ly::G_M);
+    float(*sA)[64] = reinterpret_cast<float(*)[64]>(gb + Ly::G_A);
+    int prev_hh = 0, prev_row0 = 0;
+    bool has_prev = false;
+    for (int i = grp; i < n_local; i += 2) {
+      const int u = blockIdx.x + i * gridDim.x;
+      const int st = i % kStages;
+      const uint32_t ph = (i >> 1) & 1;
+      const int hh = u % H, bc = u / H, c = bc % NT, b = bc / NT;
+      const int row0 = b * T_len + c * 64;
+      const float* sc = sSc + st * 192;
+      ok = mbar_wait(&full[st], (i / kStages) & 1, &g_status_wu) && mbar_wait(&kfull[grp], ph, &g_status_wu);
+      if (mt == 0) bulk_wait_group_read0();  // the previous w/u tiles have left sM / sA
+      if (!named_bar_and(bar_vote, kGroup, ok)) { ok = false; break; }
+      tc_fence_after();
+      {
+        // M_rc = beta_r (k_r.k_c) e^{g_r - g_c}, c < r
+        float kv[32];
+        tmem_ld_16x256b_x8(tbase + 256 * grp + lane_base, kv);
+        tc_fence_before();
+        mbar_arrive(&tfree_k[grp]);
+        const int r0 = 16 * sp + (lane >> 2), r1 = r0 + 8;
+        const float b0 = sc[r0], b1 = sc[r1], g0 = sc[64 + r0], g1 = sc[64 + r1];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int cc = 8 * j + 2 * (lane & 3);
+          const float gc0 = sc[64 + cc], gc1 = sc[64 + cc + 1];
+          float2 m0, m1;
+          m0.x = (cc < r0) ? b0 * kv[4 * j] * __expf(g0 - gc0) : 0.f;
+          m0.y = (cc + 1 < r0) ? b0 * kv[4 * j + 1] * __expf(g0 - gc1) : 0.f;
+          m1.x = (cc < r1) ? b1 * kv[4 * j + 2] * __expf(g1 - gc0) : 0.f;
+          m1.y = (cc + 1 < r1) ? b1 * kv[4 * j + 3] * __expf(g1 - gc1) : 0.f;
+          *reinterpret_cast<float2*>(&sM[r0][cc]) = m0;
+          *reinterpret_cast<float2*>(&sM[r1][cc]) = m1;
+        }
+      }
+      named_bar_sync(bar_sync, kGroup);
+      // (1) diagonal 32x32 blocks by column-parallel forward substitution
+      if (mt < 64) {
+        const int blk = mt >> 5, j = mt & 31, base = 32 * blk;
+        float x[32];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) x[q] = 0.f;
+#pragma unroll
+        for (int r = 0; r < 32; ++r) {
+          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+          for (int m = 0; m < r; m += 4) {
+            const float4 mv = *reinterpret_cast<const float4*>(&sM[base + r][base + m]);
+            s0 = fmaf(mv.x, x[m], s0);
+            s1 = fmaf(mv.y, x[m + 1], s1);
+            s2 = fmaf(mv.z, x[m + 2], s2);
+            s3 = fmaf(mv.w, x[m + 3], s3);
+          }
+          x[r] = ((r == j) ? 1.f : 0.f) - sgn * ((s0 + s1) + (s2 + s3));
+        }
+#pragma unroll
+        for (int r = 0; r < 32; ++r) {
+          sA[base + r][base + j] = x[r];
+          if (blk == 0) sA[r][32 + j] = 0.f;
+        }
+      }
+      named_bar_sync(bar_sync, kGroup);
+      // (2) T = M10 A00 (into the M00 corner of sM)
+      const int tr = mt >> 2, tc0 = (mt & 3) * 8;
+      {
+        float t8[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t8[q] = 0.f;
+#pragma unroll 8
+        for (int m = 0; m < 32; ++m) {
+          const float mv = sM[32 + tr][m];
+          const float4 a0 = *reinterpret_cast<const float4*>(&sA[m][tc0]);
+          const float4 a1 = *reinterpret_cast<const float4*>(&sA[m][tc0 + 4]);
+          t8[0] = fmaf(mv, a0.x, t8[0]); t8[1] = fmaf(mv, a0.y, t8[1]);
+          t8[2] = fmaf(mv, a0.z, t8[2]); t8[3] = fmaf(mv, a0.w, t8[3]);
+          t8[4] = fmaf(mv, a1.x, t8[4]); t8[5] = fmaf(mv, a1.y, t8[5]);
+          t8[6] = fmaf(mv, a1.z, t8[6]); t8[7] = fmaf(mv, a1.w, t8[7]);
+        }
+        named_bar_sync(bar_sync, kGroup);  // everyone done reading M00 / A00
+        *reinterpret_cast<float4*>(&sM[tr][tc0]) = make_float4(t8[0], t8[1], t8[2], t8[3]);
+        *reinterpret_cast<float4*>(&sM[tr][tc0 + 4]) = make_float4(t8[4], t8[5], t8[6], t8[7]);
+      }
+      named_bar_sync(bar_sync, kGroup);
+      // (3) A10 = -sign A11 T
+      {
+        float a8[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) a8[q] = 0.f;
+#pragma unroll 8
+        for (int m = 0; m < 32; ++m) {
+          const float av = sA[32 + tr][32 + m];
+          const float4 t0 = *reinterpret_cast<const float4*>(&sM[m][tc0]);
+          const float4 t1 = *reinterpret_cast<const float4*>(&sM[m][tc0 + 4]);
+          a8[0] = fmaf(av, t0.x, a8[0]); a8[1] = fmaf(av, t0.y, a8[1]);
+          a8[2] = fmaf(av, t0.z, a8[2]); a8[3] = fmaf(av, t0.w, a8[3]);
+          a8[4] = fmaf(av, t1.x, a8[4]); a8[5] = fmaf(av, t1.y, a8[5]);
+          a8[6] = fmaf(av, t1.z, a8[6]); a8[7] = fmaf(av, t1.w, a8[7]);
+        }
+        *reinterpret_cast<float4*>(&sA[32 + tr][tc0]) =
+            make_float4(-sgn * a8[0], -sgn * a8[1], -sgn * a8[2], -sgn * a8[3]);
+        *reinterpret_cast<float4*>(&sA[32 + tr][tc0 + 4]) =
+            make_float4(-sgn * a8[4], -sgn * a8[5], -sgn * a8[6], -sgn * a8[7]);
+      }
+      // the previous unit's W/U products have consumed the A operands
+      ok = !has_prev || mbar_wait(&ofull[grp], ph ^ 1, &g_status_wu);
+      if (!named_bar_and(bar_vote, kGroup, ok)) { ok = false; break; }
+      // (4) the MMA operands A diag(beta e^g), A diag(beta) in bf16 (+ optional fp32 A)
+      {
+        const int t = mt >> 1, s0 = (mt & 1) * 32;
+        uint8_t* aw = gb + Ly::G_AW;
+        uint8_t* au = gb + Ly::G_AU;
+#pragma unroll
+        for (int q = 0; q < 32; q += 8) {
+          float a[8];
+          *reinterpret_cast<float4*>(a) = *reinterpret_cast<const float4*>(&sA[t][s0 + q]);
+          *reinterpret_cast<float4*>(a + 4) = *reinterpret_cast<const float4*>(&sA[t][s0 + q + 4]);
+          uint4 pw, pu;
+          const float* fk = sc + 128 + s0 + q;
+          const float* fb = sc + s0 + q;
+          pw.x = pack_bf16x2(a[0] * fk[0], a[1] * fk[1]); pw.y = pack_bf16x2(a[2] * fk[2], a[3] * fk[3]);
+          pw.z = pack_bf16x2(a[4] * fk[4], a[5] * fk[5]); pw.w = pack_bf16x2(a[6] * fk[6], a[7] * fk[7]);
+          pu.x = pack_bf16x2(a[0] * fb[0], a[1] * fb[1]); pu.y = pack_bf16x2(a[2] * fb[2], a[3] * fb[3]);
+          pu.z = pack_bf16x2(a[4] * fb[4], a[5] * fb[5]); pu.w = pack_bf16x2(a[6] * fb[6], a[7] * fb[7]);
+          *reinterpret_cast<uint4*>(aw + sw128_offset(t, s0 + q, 64, 2)) = pw;
+          *reinterpret_cast<uint4*>(au + sw128_offset(t, s0 + q, 64, 2)) = pu;
+          if (a_out != nullptr) {
+            float* dst = a_out + ((long long)(row0 + t) * H + hh) * 64 + s0 + q;
+            *reinterpret_cast<float4*>(dst) = make_float4(a[0], a[1], a[2], a[3]);
+            *reinterpret_cast<float4*>(dst + 4) = make_float4(a[4], a[5], a[6], a[7]);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&afull[grp]);
+      named_bar_sync(bar_sync, kGroup);  // sA / sM reads done before they become staging
+      if (has_prev) {
+        tc_fence_after();
+        wu_epilogue<K, V>(gb, tbase, grp, sp, lane, mt, tfree_o, &tm_w, &tm_u, prev_hh, prev_row0, bar_sync);
+      }
+      has_prev = true;
+      prev_hh = hh;
+      prev_row0 = row0;
+    }
+    if (ok && has_prev) {
+      // epilogue of this group's last unit
+      const int last = grp + 2 * ((n_local - 1 - grp) / 2);
+      ok = mbar_wait(&ofull[grp], (last >> 1) & 1, &g_status_wu);
+      if (named_bar_and(bar_vote, kGroup, ok)) {
+        tc_fence_after();
+        if (mt == 0) bulk_wait_group_read0();
+        named_bar_sync(bar_sync, kGroup);
+        wu_epilogue<K, V>(gb, tbase, grp, sp, lane, mt, tfree_o, &tm_w, &tm_u, prev_hh, prev_row0, bar_sync);
+      } else {
+        ok = false;
+      }
+    }
+    if (mt == 0) bulk_wait_group0();
+  }
+
+  if (!ok) record_status(&g_status_wu, THM_ERR_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 512);
+}
+
+template <int K, int V>
+int launch(const void* k, const void* v, const float* beta, const float* g, void* w, void* u, float* a_out, int B,
+           int T_len, int H, int a_mode, cudaStream_t st) {
+  using Ly = Layout<K, V>;
+  const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int NT = T_len / 64;
+  const uint64_t rows = (uint64_t)B * T_len;
+  const uint32_t box[3] = {64u, 1u, 64u};
+  CUtensorMap tk, tv, tw, tu;
+  {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)H, rows};
+    uint64_t str[2] = {(uint64_t)K * 2, (uint64_t)H * K * 2};
+    int r = encode_tiled(&tk, dt, 3, k, dims, str, box);
+    if (r == THM_OK) r = encode_tiled(&tw, dt, 3, w, dims, str, box);
+    if (r != THM_OK) return r;
+  }
+  {
+    uint64_t dims[3] = {(uint64_t)V, (uint64_t)H, rows};
+    uint64_t str[2] = {(uint64_t)V * 2, (uint64_t)H * V * 2};
+    int r = encode_tiled(&tv, dt, 3, v, dims, str, box);
+    if (r == THM_OK) r = encode_tiled(&tu, dt, 3, u, dims, str, box);
+    if (r != THM_OK) return r;
+  }
+  auto kern = recompute_w_u_ws_kernel<K, V>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
+    return THM_ERR_CUDA;
+  const int nunits = B * NT * H;
+  const int grid = nunits < sm_count() ? nunits : sm_count();
+  kern<<<grid, kThreads, Ly::SMEM, st>>>(tk, tv, tw, tu, beta, g, a_out, T_len, H, NT, nunits,
+                                         a_mode > 0 ? 1.0f : -1.0f);
+  return check_launch();
+}
+
+}  // namespace ws
 }  // namespace wu
 }  // namespace thm
 
@@ -390,6 +806,14 @@ extern "C" int thm_recompute_w_u_fwd(const void* k, const void* v, const float* 
     return THM_ERR_ALIGNMENT;
   if ((long long)B * H > 65535) return THM_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == THM_BF16 && a_mode != 0) {
+    // In-kernel A with bf16 operands: the persistent warp-specialized kernel.
+    if (K == 64)
+      return V == 64 ? wu::ws::launch<64, 64>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, st)
+                     : wu::ws::launch<64, 128>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, st);
+    return V == 64 ? wu::ws::launch<128, 64>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, st)
+                   : wu::ws::launch<128, 128>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, st);
+  }
   if (dtype == THM_BF16)
     return wu::dispatch<__nv_bfloat16>(k, v, beta, A, g, w, u, A_out, B, T, H, K, V, a_mode, st);
   return wu::dispatch<float>(k, v, beta, A, g, w, u, A_out, B, T, H, K, V, a_mode, st);
