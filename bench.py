@@ -213,10 +213,8 @@ def run_chain(args, rank, world, device):
     ms = evs[0][0].elapsed_time(evs[-1][4])
     per = {n: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
            for j, n in enumerate(("causal_conv1d_x3", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"))}
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    from theorem_b200 import dist as D
+    ms = D.max_over_ranks(ms, device=device)
     status = _lib.device_status()
     assert status == 0, f"in-kernel wait timed out (status {status})"
     return dict(ms=ms, per_op_ms=per, clocks=clocks, tokens_per_rank=B * T, layer=layer,
@@ -462,7 +460,8 @@ def main(argv=None) -> int:
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+        from theorem_b200 import dist as D
+        D.init("nccl", timeout_s=120.0, device=device)
     from theorem_b200 import _lib
     _lib.load()
 
