@@ -17,8 +17,12 @@
 //   S     = exp(g_last) S + U_c                 registers
 //
 // k, v/u (and w) tiles of chunk c+2 stream in by TMA (double-buffered, 128-B
-// swizzle; 32-B atoms for MN-major tf32 operands) while chunk c is processed.
+// swizzle; 32-B atoms for MN-major tf32 operands) while chunk c is processed;
+// the h and v_new tiles leave through shared memory by TMA store (a row per
+// thread written straight to HBM would touch 32 rows per store instruction).
 #include <cuda_bf16.h>
+
+#include <type_traits>
 
 #include "host_util.h"
 #include "sm100.cuh"
@@ -32,51 +36,64 @@ constexpr int kThreads = 128;
 constexpr int kBT = 64;
 constexpr int kVT = 64;
 
-template <typename T, int K, int MODE>
+template <typename T, int K, int MODE, bool HB>
 struct Layout {
   static constexpr int ES = sizeof(T);
   static constexpr bool BF16 = ES == 2;
+  static constexpr int HES = HB ? 2 : 4;                      // stored h element size
   static constexpr int K_BYTES = kBT * K * ES;               // k_c: MN-major A (k^T)
   static constexpr int V_BYTES = kBT * kVT * ES;             // v_c / u_c: MN-major B
   static constexpr int W_BYTES = MODE == 1 ? kBT * K * ES : 0;  // w_c: K-major A
   static constexpr int STAGE = K_BYTES + V_BYTES + W_BYTES;
   static constexpr int S_BYTES = MODE == 1 ? K * kVT * ES : 0;  // state as MN-major B
+  // The stored h tile leaves by TMA store. In delta mode with h in the
+  // activation dtype it is the MMA copy of the state itself; otherwise a
+  // separate [K x 64] staging tile (128-B swizzle, 16-B chunks).
+  static constexpr bool H_FROM_S = MODE == 1 && (HES == ES);
+  static constexpr int HST_BYTES = H_FROM_S ? 0 : K * kVT * HES;
+  static constexpr int VN_BYTES = MODE == 1 ? kBT * kVT * ES : 0;  // v_new staging
   static constexpr int OFF_STAGE0 = 0;
   static constexpr int OFF_S = 2 * STAGE;
-  static constexpr int OFF_MISC = OFF_S + S_BYTES;
+  static constexpr int OFF_HST = OFF_S + S_BYTES;
+  static constexpr int OFF_VN = OFF_HST + HST_BYTES;
+  static constexpr int OFF_MISC = OFF_VN + VN_BYTES;
   // misc: sG [2][64] | decay factors [64] | barriers, TMEM slot
   static constexpr int SMEM = OFF_MISC + 2048 + 1024;
   static constexpr uint32_t TMEM_COLS = 128;  // U [0,64) | X [64,128)
 };
 
-// Store one 64-wide row of the state (fp32 registers) as fp32 or bf16.
-template <bool HB>
-__device__ __forceinline__ void store_state_row(void* dst, const float* S) {
-  if constexpr (HB) {
-    __nv_bfloat16* d = static_cast<__nv_bfloat16*>(dst);
+// Write one 64-wide state row (fp32 registers) into a [rows x 64] tile of
+// element type E, 128-B swizzle: 16-B chunks (layout 2) or 32-B atoms (layout 1).
+template <typename E, bool ATOM32>
+__device__ __forceinline__ void write_state_row(uint8_t* tile, int row, int rows, const float* S) {
+  if constexpr (sizeof(E) == 2) {
 #pragma unroll
-    for (int j = 0; j < 64; j += 8) {
+    for (int j = 0; j < kVT; j += 8) {
       uint4 p;
       p.x = pack_bf16x2(S[j], S[j + 1]);
       p.y = pack_bf16x2(S[j + 2], S[j + 3]);
       p.z = pack_bf16x2(S[j + 4], S[j + 5]);
       p.w = pack_bf16x2(S[j + 6], S[j + 7]);
-      *reinterpret_cast<uint4*>(d + j) = p;
+      *reinterpret_cast<uint4*>(tile + sw128_offset(row, j, rows, 2)) = p;
     }
   } else {
-    float* d = static_cast<float*>(dst);
 #pragma unroll
-    for (int j = 0; j < 64; j += 4) *reinterpret_cast<float4*>(d + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+    for (int j = 0; j < kVT; j += 4) {
+      const uint32_t off = ATOM32 ? sw128b32_offset(row, j, rows, 4) : sw128_offset(row, j, rows, 4);
+      *reinterpret_cast<float4*>(tile + off) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+    }
   }
 }
 
 template <typename T, int K, int MODE, bool HB>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_fwd_h_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                       const __grid_constant__ CUtensorMap tm_w, const float* __restrict__ g,
-                       const float* __restrict__ h0, void* __restrict__ hout, T* __restrict__ v_new,
-                       float* __restrict__ final_state, int T_len, int H, int V) {
-  using Ly = Layout<T, K, MODE>;
+                       const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_hst,
+                       const __grid_constant__ CUtensorMap tm_vn, const float* __restrict__ g,
+                       const float* __restrict__ h0, float* __restrict__ final_state, int has_vn, int T_len,
+                       int H, int V) {
+  using Ly = Layout<T, K, MODE, HB>;
+  using HT = typename std::conditional<HB, __nv_bfloat16, float>::type;
   constexpr bool kBf16 = Ly::BF16;
   constexpr uint32_t kFmt = kBf16 ? 1u : 2u;
   constexpr int kStep = kBf16 ? 16 : 8;
@@ -85,6 +102,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kIdU = make_idesc(kFmt, K, kVT, 1, 1);
   constexpr uint32_t kIdX = make_idesc(kFmt, 64, kVT, 0, 1);
   constexpr int kBox = 128 / Ly::ES;
+  constexpr int kHBox = 128 / Ly::HES;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -94,6 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar_tma = reinterpret_cast<uint64_t*>(sm + Ly::OFF_MISC + 1024);  // [2]
   uint64_t* bar_mma = bar_tma + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_tma + 4);
+  uint8_t* hst = sm + (Ly::H_FROM_S ? Ly::OFF_S : Ly::OFF_HST);  // tile the h store reads
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int vt = blockIdx.x;
@@ -118,6 +137,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int j = 0; j < kVT / kBox; ++j)
       tma_load_3d(base + Ly::K_BYTES + j * kBT * 128, &tm_v, &bar_tma[st], v0 + j * kBox, hh, row0);
+  };
+  // TMA store of the h tile of chunk c (bulk group; waited before reuse).
+  auto store_h = [&](int c) {
+    const int hrow = ((b * NT + c) * H + hh) * K;
+#pragma unroll
+    for (int j = 0; j < kVT / kHBox; ++j) tma_store_2d(&tm_hst, hst + j * K * 128, v0 + j * kHBox, hrow);
   };
 
   if (tid == 0) {
@@ -169,34 +194,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sv = sk + Ly::K_BYTES;                           // v / u tile
     const uint32_t sw = sv + Ly::V_BYTES;                           // w tile
     const float* gc = sG + st * 64;
-    const long long hoff = ((((long long)b * NT + c) * H + hh) * K + kk) * V + v0;
-    void* hdst = HB ? static_cast<void*>(static_cast<__nv_bfloat16*>(hout) + hoff)
-                    : static_cast<void*>(static_cast<float*>(hout) + hoff);
+    const int row0 = b * T_len + c * kBT;
 
     if constexpr (MODE == 1) {
-      // h[c] = state entering chunk c; S -> smem as the B operand of X = w S.
+      // The previous chunk's h / v_new tiles have left shared memory.
+      if (tid == 0) bulk_wait_group_read0();
+      __syncthreads();
+      // h[c] = state entering chunk c. S -> smem as the B operand of X = w S
+      // (and, when h is stored in the activation dtype, as the h tile).
       if (srow_ok) {
-        store_state_row<HB>(hdst, S);
-        uint8_t* ss = sm + Ly::OFF_S;
-        if constexpr (kBf16) {
-#pragma unroll
-          for (int j = 0; j < kVT; j += 8) {
-            uint4 p;
-            p.x = pack_bf16x2(S[j], S[j + 1]);
-            p.y = pack_bf16x2(S[j + 2], S[j + 3]);
-            p.z = pack_bf16x2(S[j + 4], S[j + 5]);
-            p.w = pack_bf16x2(S[j + 6], S[j + 7]);
-            *reinterpret_cast<uint4*>(ss + sw128_offset(kk, j, K, 2)) = p;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < kVT; j += 4)
-            *reinterpret_cast<float4*>(ss + sw128b32_offset(kk, j, K, 4)) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
-        }
+        write_state_row<T, !kBf16>(sm + Ly::OFF_S, kk, K, S);
+        if constexpr (!Ly::H_FROM_S) write_state_row<HT, false>(sm + Ly::OFF_HST, kk, K, S);
       }
       fence_proxy_async_smem();
       tc_fence_before();
     }
+    cp_async_wait<1>();  // this chunk's gates (committed two steps ago) have landed
     ok = mbar_wait(&bar_tma[st], (c >> 1) & 1, &g_status_h);
     ok = __syncthreads_and(ok);
     if (!ok) break;
@@ -205,6 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if constexpr (MODE == 1) {
       if (tid == 0) {
+        store_h(c);
         tc_fence_after();
 #pragma unroll
         for (int q = 0; q < K / kStep; ++q) {
@@ -222,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       pending = -1;
       tc_fence_after();
-      // v_new = u - X ; u tile <- v_new * exp(g_last - g_t)
+      // v_new = u - X -> staging tile; u tile <- v_new * exp(g_last - g_t)
       {
         float xr[kVT];
         tmem_ld32(tX + lane_off, xr);
@@ -230,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane < 16) {
           const int t = warp * 16 + lane;
           const float dec = __expf(gl - gc[t]);
-          T* vn = v_new ? v_new + ((long long)(b * T_len + c * kBT + t) * H + hh) * V + v0 : nullptr;
+          uint8_t* vn = sm + Ly::OFF_VN;
 #pragma unroll
           for (int j = 0; j < kVT; j += 8) {
             float un[8];
@@ -244,16 +258,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 un[2 * q] = f.x - xr[j + 2 * q];
                 un[2 * q + 1] = f.y - xr[j + 2 * q + 1];
               }
-              if (vn) {
-                uint4 o;
-                o.x = pack_bf16x2(un[0], un[1]); o.y = pack_bf16x2(un[2], un[3]);
-                o.z = pack_bf16x2(un[4], un[5]); o.w = pack_bf16x2(un[6], un[7]);
-                *reinterpret_cast<uint4*>(vn + j) = o;
-              }
-              uint4 s;
-              s.x = pack_bf16x2(un[0] * dec, un[1] * dec); s.y = pack_bf16x2(un[2] * dec, un[3] * dec);
-              s.z = pack_bf16x2(un[4] * dec, un[5] * dec); s.w = pack_bf16x2(un[6] * dec, un[7] * dec);
-              *p = s;
+              uint4 o;
+              o.x = pack_bf16x2(un[0], un[1]); o.y = pack_bf16x2(un[2], un[3]);
+              o.z = pack_bf16x2(un[4], un[5]); o.w = pack_bf16x2(un[6], un[7]);
+              *reinterpret_cast<uint4*>(vn + sw128_offset(t, j, kBT, 2)) = o;
+              uint4 sc;
+              sc.x = pack_bf16x2(un[0] * dec, un[1] * dec); sc.y = pack_bf16x2(un[2] * dec, un[3] * dec);
+              sc.z = pack_bf16x2(un[4] * dec, un[5] * dec); sc.w = pack_bf16x2(un[6] * dec, un[7] * dec);
+              *p = sc;
             } else {
 #pragma unroll
               for (int q = 0; q < 8; q += 4) {
@@ -263,7 +275,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 un[q + 1] = r.y - xr[j + q + 1];
                 un[q + 2] = r.z - xr[j + q + 2];
                 un[q + 3] = r.w - xr[j + q + 3];
-                if (vn) *reinterpret_cast<float4*>(vn + j + q) = make_float4(un[q], un[q + 1], un[q + 2], un[q + 3]);
+                *reinterpret_cast<float4*>(vn + sw128_offset(t, j + q, kBT, 4)) =
+                    make_float4(un[q], un[q + 1], un[q + 2], un[q + 3]);
                 *p = make_float4(un[q] * dec, un[q + 1] * dec, un[q + 2] * dec, un[q + 3] * dec);
               }
             }
@@ -282,6 +295,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // U_c = k^T (scaled v / v_new) -- A = k^T (MN-major), B = v (MN-major)
     if (tid == 0) {
+      if (MODE == 1 && has_vn) {
+#pragma unroll
+        for (int j = 0; j < kVT / kBox; ++j)
+          tma_store_3d(&tm_vn, sm + Ly::OFF_VN + j * kBT * 128, v0 + j * kBox, hh, row0);
+      }
+      if (MODE == 1) bulk_commit_group();
       tc_fence_after();
 #pragma unroll
       for (int q = 0; q < kBT / kStep; ++q) {
@@ -300,12 +319,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     pending = -1;
     tc_fence_after();
 
-    // Stage st is free: prefetch chunk c+2 (tiles by TMA, gates by plain loads).
+    // Stage st is free: prefetch chunk c+2 (tiles by TMA, gates by cp.async).
     if (c + 2 < NT) {
       last_issued = c + 2;
       if (tid == 0) issue_tma(c + 2, st);
-      if (tid < kBT) sG[st * 64 + tid] = g[(long long)(b * T_len + (c + 2) * kBT + tid) * H + hh];
+      if (tid < kBT) cp_async4(&sG[st * 64 + tid], g + (long long)(b * T_len + (c + 2) * kBT + tid) * H + hh);
     }
+    cp_async_commit();
 
     // S = exp(g_last) S + U_c
     {
@@ -316,11 +336,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (srow_ok) {
 #pragma unroll
         for (int j = 0; j < kVT; ++j) S[j] = fmaf(eg, S[j], ur[j]);
-        if constexpr (MODE == 0) store_state_row<HB>(hdst, S);
       }
     }
     tc_fence_before();
+    if constexpr (MODE == 0) {
+      // h[c] = state after chunk c, through the staging tile and a TMA store.
+      if (tid == 0) bulk_wait_group_read0();
+      __syncthreads();
+      if (srow_ok) write_state_row<HT, false>(sm + Ly::OFF_HST, kk, K, S);
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        store_h(c);
+        bulk_commit_group();
+      }
+    }
   }
+  cp_async_wait<0>();
+  if (tid == 0) bulk_wait_group0();
 
   if (ok && MODE == 1 && final_state != nullptr && srow_ok) {
     float* dst = final_state + (((long long)b * H + hh) * K + kk) * V + v0;
@@ -340,14 +373,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <typename T, int K, int MODE, bool HB>
 int launch(const void* k, const void* w, const void* v, const float* g, const float* h0, void* h, void* v_new,
            float* final_state, int B, int T_len, int H, int V, cudaStream_t st) {
-  using Ly = Layout<T, K, MODE>;
+  using Ly = Layout<T, K, MODE, HB>;
   constexpr bool bf = Ly::BF16;
   const CUtensorMapDataType dt = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   const CUtensorMapSwizzle mn_sw = bf ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   const int es = sizeof(T);
+  const int NT = T_len / kBT;
   const uint64_t rows = (uint64_t)B * T_len;
   const uint32_t box[3] = {(uint32_t)(128 / es), 1u, (uint32_t)kBT};
-  CUtensorMap tk, tv, tw;
+  CUtensorMap tk, tv, tw, th, tvn;
   {
     uint64_t dims[3] = {(uint64_t)K, (uint64_t)H, rows};
     uint64_t str[2] = {(uint64_t)K * es, (uint64_t)H * K * es};
@@ -360,13 +394,30 @@ int launch(const void* k, const void* w, const void* v, const float* g, const fl
     uint64_t dims[3] = {(uint64_t)V, (uint64_t)H, rows};
     uint64_t str[2] = {(uint64_t)V * es, (uint64_t)H * V * es};
     int r = encode_tiled(&tv, dt, 3, v, dims, str, box, mn_sw);
+    if (r == THM_OK && MODE == 1 && v_new != nullptr)
+      r = encode_tiled(&tvn, dt, 3, v_new, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    else
+      tvn = tv;  // unused
+    if (r != THM_OK) return r;
+  }
+  {
+    // h [B*NT*H*K, V] as stored; the smem tile is either the state operand
+    // (32-B atoms when fp32 activations) or the 16-B-chunk staging tile.
+    const int hes = HB ? 2 : 4;
+    uint64_t dims[2] = {(uint64_t)V, (uint64_t)B * NT * H * K};
+    uint64_t str[1] = {(uint64_t)V * hes};
+    uint32_t hbox[2] = {(uint32_t)(128 / hes), (uint32_t)K};
+    const CUtensorMapSwizzle hsw = (Ly::H_FROM_S && !bf) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+    int r = encode_tiled(&th, HB ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, h, dims,
+                         str, hbox, hsw);
     if (r != THM_OK) return r;
   }
   auto kern = chunk_fwd_h_kernel<T, K, MODE, HB>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
     return THM_ERR_CUDA;
   dim3 grid(V / kVT, B * H);
-  kern<<<grid, kThreads, Ly::SMEM, st>>>(tk, tv, tw, g, h0, h, static_cast<T*>(v_new), final_state, T_len, H, V);
+  kern<<<grid, kThreads, Ly::SMEM, st>>>(tk, tv, tw, th, tvn, g, h0, final_state, v_new != nullptr ? 1 : 0, T_len,
+                                         H, V);
   return check_launch();
 }
 

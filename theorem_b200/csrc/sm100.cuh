@@ -126,6 +126,12 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
       "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until no bulk group issued by this thread is still reading shared memory.
 __device__ __forceinline__ void bulk_wait_group_read0() {
@@ -151,6 +157,18 @@ __device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t count, bool 
       : "r"((uint32_t)pred), "r"(id), "r"(count)
       : "memory");
   return r != 0;
+}
+
+// Asynchronous 4-byte global -> shared copy (no register round trip), grouped
+// with commit / wait_group.
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's committed groups are still pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Make generic-proxy writes to shared memory visible to the async proxy
