@@ -111,3 +111,22 @@ def test_misaligned_channel_last_rejected():
     x = torch.zeros(1, 4, 13 * 8, device=DEV)[..., :-8]  # D = 96 but row stride breaks contiguity
     with pytest.raises(AssertionError):
         ops.causal_conv1d(x, torch.zeros(96, 4, device=DEV), torch.zeros(96, device=DEV), layout="bsd")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("D,S,G", [(640, 700, 128), (2048, 1024, 128), (264, 33, 0), (1024, 257, 64)])
+def test_channel_last_tma_tiles(dtype, D, S, G):
+    """TMA-tiled path: partial channel blocks (D % 256 != 0), several 256-row
+    strips, partial 32-row tiles, batch boundaries (the halo must not leak)."""
+    from theorem_b200 import ops
+    B, W = 3, 4
+    gen = torch.Generator().manual_seed(D + S + G)
+    x = torch.randn(B, S, D, generator=gen).to(dtype)
+    w = torch.randn(D, W, generator=gen) * 0.5
+    b = torch.randn(D, generator=gen) * 0.3
+    out = ops.causal_conv1d(x.to(DEV), w.to(DEV), b.to(DEV), activation="silu", layout="bsd", l2norm_group=G)
+    ref = orc.causal_conv1d(x.float(), w, b, "silu", layout="bsd")
+    if G:
+        ref = orc.l2norm(ref.reshape(B, S, D // G, G)).reshape(B, S, D)
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert_close(out.float().cpu().double(), torch.from_numpy(ref), tol, tol, f"{dtype} D={D} S={S} G={G}")

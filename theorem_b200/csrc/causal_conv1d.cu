@@ -131,6 +131,10 @@ struct Vec4<__nv_bfloat16> {
     r.y = pack_bf16x2(f[2], f[3]);
     *reinterpret_cast<uint2*>(p) = r;
   }
+  __device__ __forceinline__ void raw_from_smem(const uint8_t* p) { raw = *reinterpret_cast<const uint2*>(p); }
+  __device__ __forceinline__ static void store_smem(uint8_t* p, const float* f) {
+    store(reinterpret_cast<__nv_bfloat16*>(p), f);
+  }
 };
 template <>
 struct Vec4<float> {
@@ -139,6 +143,10 @@ struct Vec4<float> {
   __device__ __forceinline__ void to_float(float* f) const { f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; }
   __device__ __forceinline__ static void store(float* p, const float* f) {
     *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+  }
+  __device__ __forceinline__ void raw_from_smem(const uint8_t* p) { a = *reinterpret_cast<const float4*>(p); }
+  __device__ __forceinline__ static void store_smem(uint8_t* p, const float* f) {
+    store(reinterpret_cast<float*>(p), f);
   }
 };
 
@@ -290,6 +298,122 @@ __global__ void __launch_bounds__(kBsdThreads) conv_bsd_generic(const T* __restr
 }
 
 // ---------------------------------------------------------------------------
+// BSD through TMA tiles (D * sizeof(T) % 16 == 0, W <= 8): one CTA = 256
+// channels x a 256-step strip, tiles of 32 rows. Each tile and its W-1 halo
+// rows arrive by TMA from a per-batch 3-D map [B][S][D] (rows before t = 0 are
+// the map's zero fill), 3-stage ring; the output tile is staged in smem and
+// written by TMA store. 256 threads: thread = 4 channels x 8 rows; a warp
+// covers 128 consecutive channels of one row group, so a per-head L2 norm of
+// up to 128 channels is a warp shuffle reduction.
+// ---------------------------------------------------------------------------
+namespace tma {
+constexpr int kThreads = 256;
+constexpr int kCh = 256;     // channels per CTA
+constexpr int kRows = 32;    // output rows per tile
+constexpr int kStrip = 256;  // rows per CTA
+constexpr int kStages = 3;
+
+template <typename T, int W>
+struct Layout {
+  static constexpr int ES = sizeof(T);
+  static constexpr int IN_ROWS = kRows + W - 1;
+  static constexpr int IN_BYTES = IN_ROWS * kCh * ES;
+  static constexpr int IN_STRIDE = (IN_BYTES + 1023) / 1024 * 1024;
+  static constexpr int OUT_BYTES = kRows * kCh * ES;
+  static constexpr int OFF_OUT = kStages * IN_STRIDE;
+  static constexpr int OFF_BAR = OFF_OUT + 2 * OUT_BYTES;
+  static constexpr int SMEM = OFF_BAR + 64 + 1024;
+};
+
+template <typename T, int W, bool SILU, int GL>
+__global__ void __launch_bounds__(kThreads, 2)
+    conv_bsd_tma(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_o,
+                 const float* __restrict__ w, const float* __restrict__ bias, int S, int D) {
+  using Ly = Layout<T, W>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + Ly::OFF_BAR);
+  const int tid = threadIdx.x;
+  const int cg = tid & 63, rq = tid >> 6;  // channel group (4 ch), row quarter (8 rows)
+  const int c0 = blockIdx.x * kCh;
+  const int t_begin = blockIdx.y * kStrip;
+  const int b = blockIdx.z;
+  const int ntiles = min(kStrip, S - t_begin + kRows - 1) / kRows;
+  const int cc = min(c0 + 4 * cg, D - 4);  // clamp: channels past D are computed but not stored
+
+  float wr[4][W], bs[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    bs[j] = __ldg(bias + cc + j);
+#pragma unroll
+    for (int k = 0; k < W; ++k) wr[j][k] = __ldg(w + (long long)(cc + j) * W + k);
+  }
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) mbar_init(&full[i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int i) {
+    const int st = i % kStages;
+    mbar_arrive_expect_tx(&full[st], Ly::IN_ROWS * kCh * Ly::ES);
+    tma_load_3d(sm + st * Ly::IN_STRIDE, &tm_x, &full[st], c0, t_begin + i * kRows - (W - 1), b);
+  };
+  if (tid == 0)
+    for (int i = 0; i < kStages && i < ntiles; ++i) issue(i);
+
+  bool ok = true;
+  for (int i = 0; i < ntiles; ++i) {
+    const int st = i % kStages, ob = i & 1;
+    // the store that last used this output buffer (tile i-2) has read it
+    if (tid == 0 && i >= 2) bulk_wait_group_read1();
+    ok = mbar_wait(&full[st], (i / kStages) & 1, &g_status_conv);
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    const uint8_t* in = sm + st * Ly::IN_STRIDE;
+    uint8_t* out = sm + Ly::OFF_OUT + ob * Ly::OUT_BYTES;
+    // rows r0-W+1 .. r0+7 of this tile (smem row = tile row + W - 1)
+    float xr[8 + W - 1][4];
+#pragma unroll
+    for (int j = 0; j < 8 + W - 1; ++j) {
+      Vec4<T> v;
+      v.raw_from_smem(in + ((8 * rq + j) * kCh + 4 * cg) * Ly::ES);
+      v.to_float(xr[j]);
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      float o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float acc = bs[j];
+#pragma unroll
+        for (int k = 0; k < W; ++k) acc = fmaf(xr[r + k][j], wr[j][k], acc);
+        o[j] = SILU ? silu_f(acc) : acc;
+      }
+      if (GL > 0) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ss = fmaf(o[j], o[j], ss);
+#pragma unroll
+        for (int m = 1; m < GL; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+        const float rn = rsqrtf(ss + 1e-6f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] *= rn;
+      }
+      Vec4<T>::store_smem(out + ((8 * rq + r) * kCh + 4 * cg) * Ly::ES, o);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tma_store_3d(&tm_o, out, c0, t_begin + i * kRows, b);
+      bulk_commit_group();
+      if (i + kStages < ntiles) issue(i + kStages);
+    }
+  }
+  if (tid == 0) bulk_wait_group0();
+}
+}  // namespace tma
+
+// ---------------------------------------------------------------------------
 // dispatch
 // ---------------------------------------------------------------------------
 template <int W, bool SILU>
@@ -329,9 +453,36 @@ void launch_bsd(const T* x, const float* w, const float* b, T* o, int B, int D, 
   conv_bsd<T, W, SILU, GL><<<grid, kBsdThreads, 0, st>>>(x, w, b, o, S, D);
 }
 
+template <typename T, int W, bool SILU, int GL>
+int launch_bsd_tma(const T* x, const float* w, const float* b, T* o, int B, int D, int S, cudaStream_t st) {
+  using Ly = tma::Layout<T, W>;
+  const CUtensorMapDataType dt = sizeof(T) == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUtensorMap tx, to;
+  uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)B};
+  uint64_t str[2] = {(uint64_t)D * sizeof(T), (uint64_t)S * D * sizeof(T)};
+  uint32_t ibox[3] = {(uint32_t)tma::kCh, (uint32_t)Ly::IN_ROWS, 1u};
+  uint32_t obox[3] = {(uint32_t)tma::kCh, (uint32_t)tma::kRows, 1u};
+  int r = encode_tiled(&tx, dt, 3, x, dims, str, ibox, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (r == THM_OK) r = encode_tiled(&to, dt, 3, o, dims, str, obox, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (r != THM_OK) return r;
+  auto kern = tma::conv_bsd_tma<T, W, SILU, GL>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
+    return THM_ERR_CUDA;
+  dim3 grid((D + tma::kCh - 1) / tma::kCh, (S + tma::kStrip - 1) / tma::kStrip, B);
+  kern<<<grid, tma::kThreads, Ly::SMEM, st>>>(tx, to, w, b, S, D);
+  return check_launch();
+}
+
 template <typename T, bool SILU, int GL>
 int dispatch_bsd_w(const T* x, const float* w, const float* b, T* o, int B, int D, int S, int W,
                    cudaStream_t st) {
+  if ((D * (int)sizeof(T)) % 16 == 0 && D >= 4 && (W == 2 || W == 3 || W == 4)) {
+    switch (W) {
+      case 2: return launch_bsd_tma<T, 2, SILU, GL>(x, w, b, o, B, D, S, st);
+      case 3: return launch_bsd_tma<T, 3, SILU, GL>(x, w, b, o, B, D, S, st);
+      default: return launch_bsd_tma<T, 4, SILU, GL>(x, w, b, o, B, D, S, st);
+    }
+  }
   switch (W) {
     case 2: launch_bsd<T, 2, SILU, GL>(x, w, b, o, B, D, S, st); break;
     case 3: launch_bsd<T, 3, SILU, GL>(x, w, b, o, B, D, S, st); break;
