@@ -404,9 +404,11 @@ struct Layout {
   static constexpr int STAGE = KB + VB;
   static constexpr int OFF_STAGE = 0;                    // [3] k | v
   static constexpr int OFF_GRP = kStages * STAGE;        // per math group:
-  static constexpr int G_M = 0;                          //   M / T fp32 [64][64]; w staging
-  static constexpr int G_A = 16384;                      //   A fp32 [64][64];     u staging
-  static constexpr int G_AW = 32768;                     //   A diag(beta e^g) bf16, K-major
+  static constexpr int LDM = 68;                         //   row stride (floats) of M and A:
+                                                         //   4-bank shift per row, no 8-way conflicts
+  static constexpr int G_M = 0;                          //   M / T fp32 [64][68]; w staging
+  static constexpr int G_A = 64 * LDM * 4;               //   A fp32 [64][68];     u staging
+  static constexpr int G_AW = 2 * 64 * LDM * 4;          //   A diag(beta e^g) bf16, K-major
   static constexpr int G_AU = G_AW + 8192;               //   A diag(beta) bf16, K-major
   static constexpr int GRP = G_AU + 8192;
   static constexpr int OFF_SC = OFF_GRP + 2 * GRP;       // beta, g, beta*e^g [3][3][64] f32
@@ -541,42 +543,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------- tcgen05 issuer ----------------
+    // Two independent streams, issued in whatever order their inputs arrive:
+    //   KK^T(i) needs stage i loaded and unit i-2's M formation done;
+    //   W/U(i)  needs A(i) written and unit i-2's W/U read out.
     if (lane == 0) {
-      auto issue_kk = [&](int i) -> bool {
-        const int st = i % kStages, gi = i & 1;
-        if (!mbar_wait(&full[st], (i / kStages) & 1, &g_status_wu)) return false;
-        if (i >= 2 && !mbar_wait(&tfree_k[gi], ((i >> 1) & 1) ^ 1, &g_status_wu)) return false;
-        tc_fence_after();
-        const uint32_t sk = sbase + Ly::OFF_STAGE + st * Ly::STAGE;
+      int next_kk = 0, next_wu = 0;
+      uint64_t t_last = globaltimer_ns();
+      while (next_wu < n_local) {
+        bool did = false;
+        if (next_kk < n_local) {
+          const int i = next_kk, st = i % kStages, gi = i & 1;
+          if (mbar_test(&full[st], (i / kStages) & 1) &&
+              (i < 2 || mbar_test(&tfree_k[gi], ((i >> 1) & 1) ^ 1))) {
+            tc_fence_after();
+            const uint32_t sk = sbase + Ly::OFF_STAGE + st * Ly::STAGE;
 #pragma unroll
-        for (int q = 0; q < K / 16; ++q) {
-          const uint64_t d = make_sdesc(sk + (q / 4) * 8192 + (q % 4) * 32, 16, 1024);
-          mma_bf16_ss(tbase + 256 * gi, d, d, kIdKK, q > 0);
+            for (int q = 0; q < K / 16; ++q) {
+              const uint64_t d = make_sdesc(sk + (q / 4) * 8192 + (q % 4) * 32, 16, 1024);
+              mma_bf16_ss(tbase + 256 * gi, d, d, kIdKK, q > 0);
+            }
+            mma_commit(&kfull[gi]);
+            ++next_kk;
+            did = true;
+          }
         }
-        mma_commit(&kfull[gi]);
-        return true;
-      };
-      for (int i = 0; i < 2 && i < n_local && ok; ++i) ok = issue_kk(i);
-      for (int i = 0; i < n_local && ok; ++i) {
-        const int st = i % kStages, gi = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        if (!mbar_wait(&afull[gi], ph, &g_status_wu)) { ok = false; break; }
-        if (i >= 2 && !mbar_wait(&tfree_o[gi], ph ^ 1, &g_status_wu)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t sk = sbase + Ly::OFF_STAGE + st * Ly::STAGE;
-        const uint32_t sv = sk + Ly::KB;
-        const uint32_t grp = sbase + Ly::OFF_GRP + gi * Ly::GRP;
+        if (next_wu < next_kk) {
+          const int i = next_wu, st = i % kStages, gi = i & 1;
+          const uint32_t ph = (i >> 1) & 1;
+          if (mbar_test(&afull[gi], ph) && (i < 2 || mbar_test(&tfree_o[gi], ph ^ 1))) {
+            tc_fence_after();
+            const uint32_t sk = sbase + Ly::OFF_STAGE + st * Ly::STAGE;
+            const uint32_t sv = sk + Ly::KB;
+            const uint32_t grp = sbase + Ly::OFF_GRP + gi * Ly::GRP;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint64_t aw = make_sdesc(grp + Ly::G_AW + q * 32, 16, 1024);
-          const uint64_t au = make_sdesc(grp + Ly::G_AU + q * 32, 16, 1024);
-          // W = A_w k at TMEM lane 0, U = A_u v at lane 16 (interleaved M=64 accumulators)
-          mma_bf16_ss(tbase + 256 * gi + 64, aw, make_sdesc(sk + q * 2048, 8192, 1024), kIdW, q > 0);
-          mma_bf16_ss(tbase + 256 * gi + 64 + (16u << 16), au, make_sdesc(sv + q * 2048, 8192, 1024), kIdU, q > 0);
+            for (int q = 0; q < 4; ++q) {
+              const uint64_t aw = make_sdesc(grp + Ly::G_AW + q * 32, 16, 1024);
+              const uint64_t au = make_sdesc(grp + Ly::G_AU + q * 32, 16, 1024);
+              // W = A_w k at TMEM lane 0, U = A_u v at lane 16 (interleaved M=64 accumulators)
+              mma_bf16_ss(tbase + 256 * gi + 64, aw, make_sdesc(sk + q * 2048, 8192, 1024), kIdW, q > 0);
+              mma_bf16_ss(tbase + 256 * gi + 64 + (16u << 16), au, make_sdesc(sv + q * 2048, 8192, 1024), kIdU,
+                          q > 0);
+            }
+            mma_commit(&ofull[gi]);
+            mma_commit(&empty[st]);
+            ++next_wu;
+            did = true;
+          }
         }
-        mma_commit(&ofull[gi]);
-        mma_commit(&empty[st]);
-        if (i + 2 < n_local && !issue_kk(i + 2)) { ok = false; break; }
+        const uint64_t now = globaltimer_ns();
+        if (did) {
+          t_last = now;
+        } else if (now - t_last > kWaitLimitNs) {
+          record_status(&g_status_wu, THM_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
       }
     }
   } else {
@@ -587,8 +608,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = (uint32_t)(32 * sp) << 16;
     const uint32_t bar_sync = 1 + grp, bar_vote = 3 + grp;
     uint8_t* gb = sm + Ly::OFF_GRP + grp * Ly::GRP;
-    float(*sM)[64] = reinterpret_cast<float(*)[64]>(gb + Ly::G_M);
-    float(*sA)[64] = reinterpret_cast<float(*)[64]>(gb + Ly::G_A);
+    float(*sM)[Ly::LDM] = reinterpret_cast<float(*)[Ly::LDM]>(gb + Ly::G_M);
+    float(*sA)[Ly::LDM] = reinterpret_cast<float(*)[Ly::LDM]>(gb + Ly::G_A);
     int prev_hh = 0, prev_row0 = 0;
     bool has_prev = false;
     for (int i = grp; i < n_local; i += 2) {
