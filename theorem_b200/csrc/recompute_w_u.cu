@@ -382,9 +382,10 @@ int dispatch(const void* k, const void* v, const float* beta, const float* A, co
 //                 W = (A diag(beta e^g)) k   (M=64, N=K, K=64)  TMEM lane 0
 //                 U = (A diag(beta)) v       (M=64, N=V, K=64)  TMEM lane 16
 //   warps 2-5 / 6-9  two math groups taking alternate units. Per unit i:
-//               M from KK^T (TMEM) -> A = (I + sign M)^-1 as a 2x2 block
-//               inverse (two 32x32 forward substitutions, then
-//               A10 = -sign A11 M10 A00) -> the two column-scaled bf16 copies
+//               M from KK^T (TMEM) -> A = (I + sign M)^-1 by recursive 2x2
+//               blocking (four 16x16 forward substitutions, then
+//               A10 = -sign A11 M10 A00 at the 16 and then the 32 level)
+//               -> the two column-scaled bf16 copies
 //               of A as MMA operands; then the epilogue of the group's
 //               previous unit (i-2), whose products finished meanwhile:
 //               TMEM -> smem -> TMA store of w, u.
@@ -597,6 +598,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           record_status(&g_status_wu, THM_ERR_TIMEOUT);
           ok = false;
           break;
+        } else {
+          // back off: a tight poll would take issue slots from the math warp
+          // sharing this SM sub-partition
+          __nanosleep(64);
         }
       }
     }
@@ -645,14 +650,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       named_bar_sync(bar_sync, kGroup);
-      // (1) diagonal 32x32 blocks by column-parallel forward substitution
+      // (1a) four diagonal 16x16 blocks by column-parallel forward substitution
       if (mt < 64) {
-        const int blk = mt >> 5, j = mt & 31, base = 32 * blk;
-        float x[32];
+        const int blk = mt >> 4, j = mt & 15, base = 16 * blk;
+        float x[16];
 #pragma unroll
-        for (int q = 0; q < 32; ++q) x[q] = 0.f;
+        for (int q = 0; q < 16; ++q) x[q] = 0.f;
 #pragma unroll
-        for (int r = 0; r < 32; ++r) {
+        for (int r = 0; r < 16; ++r) {
           float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
           for (int m = 0; m < r; m += 4) {
@@ -664,11 +669,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           x[r] = ((r == j) ? 1.f : 0.f) - sgn * ((s0 + s1) + (s2 + s3));
         }
+        // Only the lower-triangular blocks of sA are ever written; readers
+        // below never touch the (unwritten) upper-right blocks.
 #pragma unroll
-        for (int r = 0; r < 32; ++r) {
-          sA[base + r][base + j] = x[r];
-          if (blk == 0) sA[r][32 + j] = 0.f;
+        for (int r = 0; r < 16; ++r) sA[base + r][base + j] = x[r];
+      }
+      named_bar_sync(bar_sync, kGroup);
+      // (1b) inside each 32x32 block: A_10 = -sign A_11 (M_10 A_00) on 16x16 blocks.
+      //      128 threads = 2 blocks x 16 rows x 4 column groups of 4.
+      {
+        const int p = mt >> 6, r = (mt >> 2) & 15, c4 = (mt & 3) * 4, base = 32 * p;
+        float t4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+          const float mv = sM[base + 16 + r][base + m];
+          const float4 a = *reinterpret_cast<const float4*>(&sA[base + m][base + c4]);
+          t4[0] = fmaf(mv, a.x, t4[0]); t4[1] = fmaf(mv, a.y, t4[1]);
+          t4[2] = fmaf(mv, a.z, t4[2]); t4[3] = fmaf(mv, a.w, t4[3]);
         }
+        named_bar_sync(bar_sync, kGroup);  // M_00 corners no longer read
+        *reinterpret_cast<float4*>(&sM[base + r][base + c4]) = make_float4(t4[0], t4[1], t4[2], t4[3]);
+        named_bar_sync(bar_sync, kGroup);
+        float a4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+          const float av = sA[base + 16 + r][base + 16 + m];
+          const float4 t = *reinterpret_cast<const float4*>(&sM[base + m][base + c4]);
+          a4[0] = fmaf(av, t.x, a4[0]); a4[1] = fmaf(av, t.y, a4[1]);
+          a4[2] = fmaf(av, t.z, a4[2]); a4[3] = fmaf(av, t.w, a4[3]);
+        }
+        *reinterpret_cast<float4*>(&sA[base + 16 + r][base + c4]) =
+            make_float4(-sgn * a4[0], -sgn * a4[1], -sgn * a4[2], -sgn * a4[3]);
       }
       named_bar_sync(bar_sync, kGroup);
       // (2) T = M10 A00 (into the M00 corner of sM)
@@ -677,8 +708,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         float t8[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) t8[q] = 0.f;
+        // A00 is lower triangular: rows m < 16 only touch columns < 16
 #pragma unroll 8
-        for (int m = 0; m < 32; ++m) {
+        for (int m = (tc0 >= 16 ? 16 : 0); m < 32; ++m) {
           const float mv = sM[32 + tr][m];
           const float4 a0 = *reinterpret_cast<const float4*>(&sA[m][tc0]);
           const float4 a1 = *reinterpret_cast<const float4*>(&sA[m][tc0 + 4]);
@@ -697,8 +729,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         float a8[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) a8[q] = 0.f;
+        // A11 is lower triangular: rows tr < 16 only have columns m < 16
 #pragma unroll 8
-        for (int m = 0; m < 32; ++m) {
+        for (int m = 0; m < (tr < 16 ? 16 : 32); ++m) {
           const float av = sA[32 + tr][32 + m];
           const float4 t0 = *reinterpret_cast<const float4*>(&sM[m][tc0]);
           const float4 t1 = *reinterpret_cast<const float4*>(&sM[m][tc0 + 4]);
@@ -725,6 +758,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           float a[8];
           *reinterpret_cast<float4*>(a) = *reinterpret_cast<const float4*>(&sA[t][s0 + q]);
           *reinterpret_cast<float4*>(a + 4) = *reinterpret_cast<const float4*>(&sA[t][s0 + q + 4]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a[e] = (s0 + q + e <= t) ? a[e] : 0.f;  // upper triangle unwritten
           uint4 pw, pu;
           const float* fk = sc + 128 + s0 + q;
           const float* fb = sc + s0 + q;
