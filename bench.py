@@ -416,9 +416,13 @@ def profile_op(args) -> int:
     k = ops.causal_conv1d(xk, cw[1], cb[1], "silu", "bsd", K).view(B, T, H, K)
     v = ops.causal_conv1d(xv, cw[2], cb[2], "silu", "bsd", 0).view(B, T, H, V)
     w, u = ops.recompute_w_u(k, v, beta, None, gate, a_mode=1)
-    h, vn, _ = ops.chunk_fwd_h(k, u, gate, w=w, mode=1, want_v_new=True)
+    h, vn, _ = ops.chunk_fwd_h(k, u, gate, w=w, mode=1, want_v_new=True, h_dtype=torch.bfloat16)
+    h32 = h.float() if args.op == "chunk_fwd_o_hf32" else None
+    xb = xq.float().reshape(B, T, H * K).transpose(1, 2).contiguous() if args.op == "causal_conv1d_bds" else None
     fns = {
         "causal_conv1d": lambda: ops.causal_conv1d(xq, cw[0], cb[0], "silu", "bsd", K),
+        "causal_conv1d_bds": lambda: ops.causal_conv1d(xb, cw[0], cb[0], "silu", "bds"),
+        "chunk_fwd_o_hf32": lambda: ops.chunk_fwd_o(q, k, vn, gate, h32, K ** -0.5),
         "recompute_w_u": lambda: ops.recompute_w_u(k, v, beta, None, gate, a_mode=1, w=w, u=u),
         "chunk_fwd_h": lambda: ops.chunk_fwd_h(k, u, gate, w=w, mode=1, h=h, v_new=vn),
         "chunk_fwd_o": lambda: ops.chunk_fwd_o(q, k, vn, gate, h, K ** -0.5),
@@ -439,7 +443,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-per-op", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--op", choices=["causal_conv1d", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"],
+    ap.add_argument("--op", choices=["causal_conv1d", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o",
+                                     "chunk_fwd_o_hf32", "causal_conv1d_bds"],
                     help="profiling mode: launch one op (bf16, chain settings) --iters times and exit")
     ap.add_argument("--shape", default="2,4096,16,128,128", help="B,T,H,K,V for --op")
     ap.add_argument("--iters", type=int, default=3)
