@@ -266,7 +266,7 @@ def time_op(fn, iters=20, warm=3, flush=None):
     ts = []
     for _ in range(iters):
         if flush is not None:
-            flush.zero_()
+            flush()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         fn()
@@ -282,7 +282,16 @@ def per_op(device, pk):
     import torch.nn.functional as F
     from theorem_b200 import ops
     out = {}
-    flush = torch.empty(512 * 1024 * 1024 // 4, device=device)  # 512 MB > 126 MB L2
+    # L2 flush between timed iterations: write 512 MB (> 126 MB L2), then read another 256 MB,
+    # so that the L2 holds no line of the op's data and no dirty line whose write-back would be
+    # charged to the op's own DRAM traffic.
+    wbuf = torch.empty(512 * 1024 * 1024 // 4, device=device)
+    rbuf = torch.zeros(256 * 1024 * 1024 // 4, device=device)
+    sink = torch.empty((), device=device)
+
+    def flush():
+        wbuf.zero_()
+        torch.sum(rbuf, dim=0, out=sink)
     g = torch.Generator(device=device).manual_seed(7)
 
     def frac(bytes_, flops, us, tc_peak):

@@ -115,3 +115,20 @@ def test_warp_specialized_many_units_per_cta():
     # repeated calls give identical results (no state leaks between launches)
     o2 = ops.chunk_fwd_o(d["q"].to(DEV), d["k"].to(DEV), d["v"].to(DEV), d["g"].to(DEV), h.to(DEV), K ** -0.5)
     assert torch.equal(o, o2)
+
+
+@pytest.mark.parametrize("K", [64, 128])
+def test_fp32_state_keeps_fp32_accuracy(K):
+    """bf16 q/k with an fp32 h and v = 0: o = scale e^{g_t} q h. The kernel splits h
+    into bf16 hi + lo, so the only error left is the bf16 rounding of o itself."""
+    from theorem_b200 import ops
+    B, T, H, V = 1, 512, 2, 128
+    d = deltanet_inputs(B, T, H, K, V, seed=31 + K)
+    gen = torch.Generator().manual_seed(5)
+    h = torch.randn(B, T // 64, H, K, V, generator=gen) * 0.3
+    v0 = torch.zeros(B, T, H, V, dtype=torch.bfloat16)
+    o = ops.chunk_fwd_o(d["q"].to(DEV), d["k"].to(DEV), v0.to(DEV), d["g"].to(DEV), h.to(DEV), K ** -0.5)
+    ref = torch.from_numpy(orc.chunk_fwd_o(d["q"].float(), d["k"].float(), v0.float(), d["g"], h, K ** -0.5))
+    err = (o.float().cpu().double() - ref).abs()
+    bound = 2.0 ** -8 * ref.abs() + 1e-6
+    assert bool((err <= bound).all()), f"max excess {float((err - bound).max())}"

@@ -651,6 +651,332 @@ int launch(const void* q, const void* k, const void* v, const float* g, const vo
 }
 
 }  // namespace ws
+
+// ===========================================================================
+// Persistent warp-specialized variant for bf16 q/k/v/o with fp32 states h
+// (the reference's h is fp32). Units are (b, c, h, 64-column
+// V tile) with the V tile fastest, so the tiles of one (b, c, h) run on
+// neighbouring CTAs at the same time and share the q, k lines through L2.
+//
+// The fp32 h tile is split on the fly into two bf16 tiles, hi = bf16(h) and
+// lo = bf16(h - hi), and G = q hi + q lo runs in kind::f16. q is exact in bf16,
+// so G carries about 16 significant bits of h (|h - hi - lo| <= 2^-16 |h|),
+// more than the 10 of a tf32 product, at the tensor cost of one tf32 product.
+//   warp 0     TMA producer: q, k, v tile, fp32 h tile + gates, 2-stage ring
+//   warp 1     tcgen05 issuer (one thread), per unit i:
+//                L(i-1) = P v       once P(i-1) is in smem
+//                S(i)   = q k^T     M=64, N=64, K=K   -> TMEM [i%2] cols 0..63
+//                G(i)   = q hi + q lo once hi/lo(i) is in smem -> [i%2] lane 16
+//   warps 2-5  P(i) = tril(S e^{g_t-g_s}) and the epilogue o = scale (L + e^{g_t} G)
+//   warps 6-9  hi/lo(i) from the fp32 tile (single buffer, freed by G(i-1))
+// ===========================================================================
+namespace ws32 {
+
+constexpr int kThreads = 320;
+constexpr int kMath = 128;
+constexpr int kConv = 128;
+constexpr int kVT = 64;
+
+template <int K>
+struct Layout {
+  static constexpr int Q_BYTES = 64 * K * 2;          // [64 x K] bf16, K-major SW128
+  static constexpr int V_BYTES = 64 * kVT * 2;        // [64 x 64] bf16, MN-major SW128
+  static constexpr int H32_BYTES = K * kVT * 4;       // [K x 64] fp32, row-major (no swizzle)
+  static constexpr int OFF_Q = 0, OFF_K = Q_BYTES, OFF_V = 2 * Q_BYTES, OFF_H32 = 2 * Q_BYTES + V_BYTES;
+  static constexpr int STAGE = OFF_H32 + H32_BYTES;
+  static constexpr int HL_BYTES = K * kVT * 2;        // [K x 64] bf16, MN-major SW128
+  static constexpr int OFF_HI = 2 * STAGE, OFF_LO = OFF_HI + HL_BYTES;
+  static constexpr int P_BYTES = 64 * 64 * 2;
+  static constexpr int OFF_P = OFF_LO + HL_BYTES;
+  static constexpr int O_BYTES = 64 * kVT * 2;
+  static constexpr int OFF_O = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_G = OFF_O + O_BYTES;       // gates [2][64] f32
+  static constexpr int OFF_EG = OFF_G + 512;          // scale e^g [2][64] f32
+  static constexpr int OFF_BAR = OFF_EG + 512;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static_assert(STAGE % 1024 == 0 && HL_BYTES % 1024 == 0, "1024-B aligned tiles");
+};
+
+template <int K>
+__global__ void __launch_bounds__(kThreads, 1)
+    chunk_fwd_o_ws32_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_h,
+                            const __grid_constant__ CUtensorMap tm_o, const float* __restrict__ g, float scale,
+                            int T_len, int H, int NT, int NVT, int nunits) {
+  using Ly = Layout<K>;
+  constexpr uint32_t kIdS = make_idesc(1u, 64, 64, 0, 0);
+  constexpr uint32_t kIdG = make_idesc(1u, 64, kVT, 0, 1);
+  constexpr uint32_t kIdL = make_idesc(1u, 64, kVT, 0, 1);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(sm);
+  float* sGate = reinterpret_cast<float*>(sm + Ly::OFF_G);
+  float* sEg = reinterpret_cast<float*>(sm + Ly::OFF_EG);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::OFF_BAR);
+  uint64_t* full = bars;        // [2] TMA stage loaded (+ gates written)
+  uint64_t* empty = bars + 2;   // [2] stage consumed (tensor core and converters)
+  uint64_t* sfull = bars + 4;   // [2] S in TMEM
+  uint64_t* pfull = bars + 6;   // [2] P in smem
+  uint64_t* ofull = bars + 8;   // [2] L, G in TMEM
+  uint64_t* tfree = bars + 10;  // [2] TMEM buffer read out
+  uint64_t* hready = bars + 12; // hi/lo tiles written
+  uint64_t* gdone = bars + 13;  // G read the hi/lo tiles
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full[i], 33);
+      mbar_init(&empty[i], 1);
+      mbar_init(&sfull[i], 1);
+      mbar_init(&pfull[i], kMath);
+      mbar_init(&ofull[i], 1);
+      mbar_init(&tfree[i], kMath);
+    }
+    mbar_init(hready, kConv);
+    mbar_init(gdone, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    int i = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++i) {
+      const int st = i & 1;
+      if (i >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&empty[st], ((i >> 1) & 1) ^ 1, &g_status_o));
+        if (!ok) break;
+      }
+      const int vt = u % NVT, r = u / NVT, hh = r % H, bc = r / H, c = bc % NT, b = bc / NT;
+      const int row0 = b * T_len + c * 64;
+      float* gs = sGate + st * 64;
+      gs[lane] = g[(long long)(row0 + lane) * H + hh];
+      gs[lane + 32] = g[(long long)(row0 + lane + 32) * H + hh];
+      if (lane == 0) {
+        uint8_t* stg = sm + st * Ly::STAGE;
+        mbar_arrive_expect_tx(&full[st], Ly::STAGE);
+#pragma unroll
+        for (int j = 0; j < K / 64; ++j) {
+          tma_load_3d(stg + Ly::OFF_Q + j * 8192, &tm_q, &full[st], j * 64, hh, row0);
+          tma_load_3d(stg + Ly::OFF_K + j * 8192, &tm_k, &full[st], j * 64, hh, row0);
+        }
+        tma_load_3d(stg + Ly::OFF_V, &tm_v, &full[st], vt * kVT, hh, row0);
+        tma_load_2d(stg + Ly::OFF_H32, &tm_h, &full[st], vt * kVT, ((b * NT + c) * H + hh) * K);
+      }
+      mbar_arrive(&full[st]);
+    }
+  } else if (warp == 1) {
+    // ---------------- tcgen05 issuer ----------------
+    if (lane == 0) {
+      int i = 0;
+      int u = blockIdx.x;
+      while (true) {
+        const bool has = u < nunits;
+        if (i >= 1) {
+          // L(i-1) = P v: frees the stage of unit i-1 when done.
+          const int j = i - 1, sj = j & 1;
+          if (!mbar_wait(&pfull[sj], (j >> 1) & 1, &g_status_o)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t stg = sbase + sj * Ly::STAGE;
+          const uint32_t tL = tbase + 128 * sj + 64;
+          const uint32_t sp = sbase + Ly::OFF_P + sj * Ly::P_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16_ss(tL, make_sdesc(sp + kk * 32, 16, 1024), make_sdesc(stg + Ly::OFF_V + kk * 2048, 8192, 1024),
+                        kIdL, kk > 0);
+          mma_commit(&ofull[sj]);
+          mma_commit(&empty[sj]);
+        }
+        if (!has) break;
+        const int st = i & 1;
+        const uint32_t ph = (i >> 1) & 1;
+        if (!mbar_wait(&full[st], ph, &g_status_o)) { ok = false; break; }
+        if (i >= 2 && !mbar_wait(&tfree[st], ph ^ 1, &g_status_o)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t stg = sbase + st * Ly::STAGE;
+        const uint32_t tS = tbase + 128 * st, tG = tS + 64 + (16u << 16);
+#pragma unroll
+        for (int kk = 0; kk < K / 16; ++kk) {
+          const uint32_t off = (kk / 4) * 8192 + (kk % 4) * 32;
+          mma_bf16_ss(tS, make_sdesc(stg + Ly::OFF_Q + off, 16, 1024), make_sdesc(stg + Ly::OFF_K + off, 16, 1024),
+                      kIdS, kk > 0);
+        }
+        mma_commit(&sfull[st]);
+        if (!mbar_wait(hready, i & 1, &g_status_o)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < K / 16; ++kk) {
+          const uint64_t qd = make_sdesc(stg + Ly::OFF_Q + (kk / 4) * 8192 + (kk % 4) * 32, 16, 1024);
+          mma_bf16_ss(tG, qd, make_sdesc(sbase + Ly::OFF_HI + kk * 2048, Ly::HL_BYTES, 1024), kIdG, kk > 0);
+          mma_bf16_ss(tG, qd, make_sdesc(sbase + Ly::OFF_LO + kk * 2048, Ly::HL_BYTES, 1024), kIdG, 1);
+        }
+        mma_commit(gdone);
+        ++i;
+        u += gridDim.x;
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------- math warps: P and epilogue ----------------
+    const int mt = tid - 64;
+    const int sp = warp & 3;  // TMEM subpartition this warp may access
+    const uint32_t lane_base = (uint32_t)(32 * sp) << 16;
+    int i = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++i) {
+      const int st = i & 1;
+      const uint32_t ph = (i >> 1) & 1;
+      const int vt = u % NVT, r = u / NVT, hh = r % H, bc = r / H, c = bc % NT, b = bc / NT;
+      const int row0 = b * T_len + c * 64;
+      const float* gs = sGate + st * 64;
+      float* eg = sEg + st * 64;
+      ok = mbar_wait(&full[st], ph, &g_status_o) && mbar_wait(&sfull[st], ph, &g_status_o);
+      if (!named_bar_and(2, kMath, ok)) { ok = false; break; }
+      tc_fence_after();
+      {
+        float sv[32];
+        tmem_ld_16x256b_x8(tbase + 128 * st + lane_base, sv);
+        const int r0 = 16 * sp + (lane >> 2), r1 = r0 + 8;
+        const float g0 = gs[r0], g1 = gs[r1];
+        uint8_t* pbuf = sm + Ly::OFF_P + st * Ly::P_BYTES;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int cc = 8 * j + 2 * (lane & 3);
+          const float gc0 = gs[cc], gc1 = gs[cc + 1];
+          const float p00 = (cc <= r0) ? sv[4 * j] * __expf(g0 - gc0) : 0.f;
+          const float p01 = (cc + 1 <= r0) ? sv[4 * j + 1] * __expf(g0 - gc1) : 0.f;
+          const float p10 = (cc <= r1) ? sv[4 * j + 2] * __expf(g1 - gc0) : 0.f;
+          const float p11 = (cc + 1 <= r1) ? sv[4 * j + 3] * __expf(g1 - gc1) : 0.f;
+          *reinterpret_cast<uint32_t*>(pbuf + sw128_offset(r0, cc, 64, 2)) = pack_bf16x2(p00, p01);
+          *reinterpret_cast<uint32_t*>(pbuf + sw128_offset(r1, cc, 64, 2)) = pack_bf16x2(p10, p11);
+        }
+        if (mt < 64) eg[mt] = __expf(gs[mt]) * scale;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&pfull[st]);
+
+      ok = mbar_wait(&ofull[st], ph, &g_status_o);
+      if (!named_bar_and(2, kMath, ok)) { ok = false; break; }
+      tc_fence_after();
+      if (mt == 0) bulk_wait_group_read0();  // previous o tile has left smem
+      named_bar_sync(1, kMath);
+      {
+        // o = scale L + e^{g_t} scale G for rows r0, r0 + 8, packed bf16 pairs
+        const int r0 = 16 * sp + (lane >> 2), r1 = r0 + 8;
+        const float e0 = eg[r0], e1 = eg[r1];
+        const uint32_t swz = (uint32_t)((lane >> 2) & 7);
+        const uint32_t tL = tbase + 128 * st + 64 + lane_base;
+        float lv[32], gv[32];
+        tmem_ld_16x256b_x8(tL, lv);
+        tmem_ld_16x256b_x8(tL + (16u << 16), gv);
+        uint8_t* box = sm + Ly::OFF_O;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t off = (((uint32_t)j ^ swz) << 4) + (uint32_t)(lane & 3) * 4;
+          *reinterpret_cast<uint32_t*>(box + r0 * 128 + off) =
+              pack_bf16x2(fmaf(lv[4 * j], scale, gv[4 * j] * e0), fmaf(lv[4 * j + 1], scale, gv[4 * j + 1] * e0));
+          *reinterpret_cast<uint32_t*>(box + r1 * 128 + off) =
+              pack_bf16x2(fmaf(lv[4 * j + 2], scale, gv[4 * j + 2] * e1), fmaf(lv[4 * j + 3], scale, gv[4 * j + 3] * e1));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tfree[st]);
+      fence_proxy_async_smem();
+      named_bar_sync(1, kMath);
+      if (mt == 0) {
+        tma_store_3d(&tm_o, sm + Ly::OFF_O, vt * kVT, hh, row0);
+        bulk_commit_group();
+      }
+    }
+    if (mt == 0) bulk_wait_group0();
+  } else {
+    // ---------------- converters: fp32 h tile -> bf16 hi, lo ----------------
+    const int ct = tid - 192;
+    uint8_t* hi = sm + Ly::OFF_HI;
+    uint8_t* lo = sm + Ly::OFF_LO;
+    int i = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++i) {
+      const int st = i & 1;
+      ok = mbar_wait(&full[st], (i >> 1) & 1, &g_status_o) && (i == 0 || mbar_wait(gdone, (i - 1) & 1, &g_status_o));
+      if (!named_bar_and(3, kConv, ok)) { ok = false; break; }
+      const float* h32 = reinterpret_cast<const float*>(sm + st * Ly::STAGE + Ly::OFF_H32);
+#pragma unroll 4
+      for (int it = 0; it < K * kVT / 4 / kConv; ++it) {
+        const int idx = it * kConv + ct;           // float4 index: 16 per 64-column row
+        const int rr = idx >> 4, c4 = (idx & 15) * 4;
+        const float4 x = *reinterpret_cast<const float4*>(h32 + rr * kVT + c4);
+        const __nv_bfloat162 h01 = __floats2bfloat162_rn(x.x, x.y), h23 = __floats2bfloat162_rn(x.z, x.w);
+        const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+        const __nv_bfloat162 l01 = __floats2bfloat162_rn(x.x - f01.x, x.y - f01.y);
+        const __nv_bfloat162 l23 = __floats2bfloat162_rn(x.z - f23.x, x.w - f23.y);
+        const uint32_t off = sw128_offset(rr, c4, K, 2);
+        *reinterpret_cast<uint2*>(hi + off) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+        *reinterpret_cast<uint2*>(lo + off) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(hready);
+    }
+  }
+
+  if (!ok) record_status(&g_status_o, THM_ERR_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 256);
+}
+
+template <int K>
+int launch(const void* q, const void* k, const void* v, const float* g, const float* hst, void* o, float scale,
+           int B, int T_len, int H, int V, cudaStream_t st) {
+  using Ly = Layout<K>;
+  const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int NT = T_len / 64;
+  const uint64_t rows = (uint64_t)B * T_len;
+  const uint32_t box[3] = {64u, 1u, 64u};
+  CUtensorMap tq, tk, tv, th, to;
+  {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)H, rows};
+    uint64_t str[2] = {(uint64_t)K * 2, (uint64_t)H * K * 2};
+    int r = encode_tiled(&tq, dt, 3, q, dims, str, box);
+    if (r == THM_OK) r = encode_tiled(&tk, dt, 3, k, dims, str, box);
+    if (r != THM_OK) return r;
+  }
+  {
+    uint64_t dims[3] = {(uint64_t)V, (uint64_t)H, rows};
+    uint64_t str[2] = {(uint64_t)V * 2, (uint64_t)H * V * 2};
+    int r = encode_tiled(&tv, dt, 3, v, dims, str, box);
+    if (r == THM_OK) r = encode_tiled(&to, dt, 3, o, dims, str, box);
+    if (r != THM_OK) return r;
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)V, (uint64_t)B * NT * H * K};
+    uint64_t str[1] = {(uint64_t)V * 4};
+    uint32_t hbox[2] = {(uint32_t)kVT, (uint32_t)K};
+    int r = encode_tiled(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, hst, dims, str, hbox, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (r != THM_OK) return r;
+  }
+  auto kern = chunk_fwd_o_ws32_kernel<K>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
+    return THM_ERR_CUDA;
+  const int NVT = V / kVT;
+  const long long nu = (long long)B * NT * H * NVT;
+  if (nu > 0x7fffffffLL) return THM_ERR_UNSUPPORTED;
+  const int nunits = (int)nu;
+  const int grid = nunits < sm_count() ? nunits : sm_count();
+  kern<<<grid, kThreads, Ly::SMEM, st>>>(tq, tk, tv, th, to, g, scale, T_len, H, NT, NVT, nunits);
+  return check_launch();
+}
+
+}  // namespace ws32
 }  // namespace chunk_o
 }  // namespace thm
 
@@ -681,8 +1007,9 @@ extern "C" int thm_chunk_fwd_o_fwd(const void* q, const void* k, const void* v, 
   }
   const float* hf = static_cast<const float*>(h);
   if (dtype == THM_BF16) {
-    return K == 64 ? chunk_o::launch<__nv_bfloat16, 64>(q, k, v, g, hf, o, scale, B, T, H, V, st)
-                   : chunk_o::launch<__nv_bfloat16, 128>(q, k, v, g, hf, o, scale, B, T, H, V, st);
+    // fp32 state, bf16 activations: persistent kernel with the hi/lo split of h.
+    return K == 64 ? chunk_o::ws32::launch<64>(q, k, v, g, hf, o, scale, B, T, H, V, st)
+                   : chunk_o::ws32::launch<128>(q, k, v, g, hf, o, scale, B, T, H, V, st);
   }
   return K == 64 ? chunk_o::launch<float, 64>(q, k, v, g, hf, o, scale, B, T, H, V, st)
                  : chunk_o::launch<float, 128>(q, k, v, g, hf, o, scale, B, T, H, V, st);
