@@ -58,7 +58,7 @@ def test_config1_silu_fp32_within_1em4():
 
 
 @pytest.mark.parametrize("W", [1, 2, 3, 4, 5, 6, 7, 8, 9, 13])
-@pytest.mark.parametrize("S", [1, 3, 4, 12, 37, 64, 132])
+@pytest.mark.parametrize("S", [1, 3, 4, 12, 37, 64, 132, 260, 1028, 2052])
 def test_bds_edge_sizes(W, S):
     from theorem_b200 import ops
     x, w, b = _baseline_conv_inputs(2, 24, S, W, 100 * W + S)

@@ -7,9 +7,9 @@
 //
 //   out[b,d,t] = act(bias[d] + sum_{k<W} weight[d,k] * x[b,d,t-W+1+k])
 //
-// BDS ([B,D,S], S contiguous, fp32): one thread = 8 consecutive outputs of a
-//   row, float4 loads/stores; the halo comes from the neighbouring lane by
-//   warp shuffle (lane 0 reads it from memory).
+// BDS ([B,D,S], S contiguous, fp32): copy-shaped float4 access (each warp
+//   instruction covers 512 contiguous bytes of a row); the halo comes from
+//   the neighbouring lane by warp shuffle (lane 0 reads it from memory).
 // BSD ([B,S,D], D contiguous, fp32/bf16): one thread = 4 consecutive channels
 //   x a 256-step time strip, software-pipelined in tiles of 8 rows; 8-byte
 //   (bf16) or 16-byte (fp32) loads (a warp covers 128 consecutive channels),
@@ -32,7 +32,73 @@ __device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + _
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
 // ---------------------------------------------------------------------------
-// BDS, fp32, S % 4 == 0, W <= 8
+// BDS, fp32, S % 4 == 0, W <= 5: copy-shaped access. CTA (row, chunk) of a
+// [B*D, S] view; each warp owns 64 consecutive float4 of one row and thread
+// `lane` takes float4 base + 32 j + lane (j = 0, 1), so every load and store
+// instruction of a warp covers 512 contiguous bytes. The W-1 <= 4 inputs
+// before a float4 are the previous float4: lane-1's (shuffle), lane 31's of
+// the previous j, or (lane 0, j = 0) one extra load; zeros at the row start.
+// d and the W weights are uniform per CTA.
+// ---------------------------------------------------------------------------
+constexpr int kBdsThreads = 128;
+constexpr int kBdsNJ = 2;
+constexpr int kBdsQ = kBdsThreads * kBdsNJ;  // float4 per CTA
+
+template <int W, bool SILU>
+__global__ void __launch_bounds__(kBdsThreads) conv_bds_f4(const float* __restrict__ x, const float* __restrict__ w,
+                                                          const float* __restrict__ bias, float* __restrict__ out,
+                                                          int D, int S) {
+  static_assert(W >= 1 && W <= 5, "one previous float4 holds the halo");
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int row = blockIdx.x;
+  const int d = row % D;
+  const int nq = S >> 2;
+  const int base = blockIdx.y * kBdsQ + wid * (32 * kBdsNJ);
+  const float4* xr = reinterpret_cast<const float4*>(x + (long long)row * S);
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 c[kBdsNJ];
+#pragma unroll
+  for (int j = 0; j < kBdsNJ; ++j) {
+    const int q = base + 32 * j + lane;
+    c[j] = q < nq ? __ldg(xr + q) : z4;
+  }
+  const float4 pm = (lane == 0 && base > 0 && base <= nq) ? __ldg(xr + base - 1) : z4;
+  float wk[W];
+#pragma unroll
+  for (int k = 0; k < W; ++k) wk[k] = __ldg(w + (long long)d * W + k);
+  const float bd = __ldg(bias + d);
+  float4* orow = reinterpret_cast<float4*>(out + (long long)row * S);
+#pragma unroll
+  for (int j = 0; j < kBdsNJ; ++j) {
+    float4 p = make_float4(__shfl_up_sync(0xffffffffu, c[j].x, 1), __shfl_up_sync(0xffffffffu, c[j].y, 1),
+                           __shfl_up_sync(0xffffffffu, c[j].z, 1), __shfl_up_sync(0xffffffffu, c[j].w, 1));
+    if (j > 0) {
+      const float4& cp = c[j > 0 ? j - 1 : 0];
+      const float4 l31 = make_float4(__shfl_sync(0xffffffffu, cp.x, 31), __shfl_sync(0xffffffffu, cp.y, 31),
+                                     __shfl_sync(0xffffffffu, cp.z, 31), __shfl_sync(0xffffffffu, cp.w, 31));
+      if (lane == 0) p = l31;
+    } else if (lane == 0) {
+      p = pm;
+    }
+    const int q = base + 32 * j + lane;
+    if (q >= nq) continue;
+    const float v[8] = {p.x, p.y, p.z, p.w, c[j].x, c[j].y, c[j].z, c[j].w};
+    float o[4];
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      float acc = bd;
+#pragma unroll
+      for (int k = 0; k < W; ++k) acc = fmaf(v[4 + jj - (W - 1) + k], wk[k], acc);
+      o[jj] = SILU ? silu_f(acc) : acc;
+    }
+    orow[q] = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// BDS, fp32, S % 4 == 0, 6 <= W <= 8: one thread = 8 consecutive outputs of a
+// row, float4 loads/stores; the halo comes from the neighbouring lane by warp
+// shuffle (lane 0 reads it from memory).
 // ---------------------------------------------------------------------------
 template <int W, bool SILU>
 __global__ void __launch_bounds__(256) conv_bds_vec8(const float* __restrict__ x, const float* __restrict__ w,
@@ -52,9 +118,6 @@ __global__ void __launch_bounds__(256) conv_bds_vec8(const float* __restrict__ x
   const bool has_hi = (t0 + 4) < S;
   float4 c0 = ldg4(xr + t0);
   float4 c1 = has_hi ? ldg4(xr + t0 + 4) : z4;
-  // The W-1 values before t0 are the previous segment's outputs' inputs: take
-  // them from lane-1 when it holds the previous segment of the same row,
-  // else (lane 0) from memory, else (row start) zeros.
   float pv[8] = {__shfl_up_sync(0xffffffffu, c0.x, 1), __shfl_up_sync(0xffffffffu, c0.y, 1),
                  __shfl_up_sync(0xffffffffu, c0.z, 1), __shfl_up_sync(0xffffffffu, c0.w, 1),
                  __shfl_up_sync(0xffffffffu, c1.x, 1), __shfl_up_sync(0xffffffffu, c1.y, 1),
@@ -419,16 +482,21 @@ __global__ void __launch_bounds__(kThreads, 2)
 template <int W, bool SILU>
 void launch_bds_vec(const float* x, const float* w, const float* b, float* o, int B, int D, int S,
                     cudaStream_t st) {
-  const int nseg_row = (S + 7) / 8;
-  const long long total = (long long)B * D * nseg_row;
-  const unsigned blocks = (unsigned)((total + 255) / 256);
-  conv_bds_vec8<W, SILU><<<blocks, 256, 0, st>>>(x, w, b, o, D, S, total, nseg_row);
+  if constexpr (W <= 5) {
+    const dim3 grid((unsigned)(B * D), (unsigned)((S / 4 + kBdsQ - 1) / kBdsQ));
+    conv_bds_f4<W, SILU><<<grid, kBdsThreads, 0, st>>>(x, w, b, o, D, S);
+  } else {
+    const int nseg_row = (S + 7) / 8;
+    const long long total = (long long)B * D * nseg_row;
+    conv_bds_vec8<W, SILU><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(x, w, b, o, D, S, total, nseg_row);
+  }
 }
 
 template <bool SILU>
 int dispatch_bds(const float* x, const float* w, const float* b, float* o, int B, int D, int S, int W,
                  cudaStream_t st) {
-  const bool vec = (S % 4 == 0) && W <= 8 && aligned16(x) && aligned16(o);
+  const bool grid_ok = W > 5 || ((long long)B * D <= 0x7fffffffLL && (S / 4 + kBdsQ - 1) / kBdsQ <= 65535);
+  const bool vec = (S % 4 == 0) && W <= 8 && aligned16(x) && aligned16(o) && grid_ok;
   if (!vec) {
     const long long total = (long long)B * D * S;
     conv_bds_scalar<SILU><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(x, w, b, o, D, S, W, total);
