@@ -153,6 +153,7 @@ def chain_bytes(B, T, H, K, V, W):
         "recompute_w_u": 2 * act_k + 2 * act_v + 2 * rows * 4,      # k,v in; w,u out; beta,g
         "chunk_fwd_h": 2 * act_k + act_v + rows * 4 + hbytes + act_v,  # k,w,u,g in; h, v_new out
         "chunk_fwd_o": 2 * act_k + act_v + rows * 4 + hbytes + act_v,  # q,k,v_new,g,h in; o out
+        "gated_delta_ho": 3 * act_k + act_v + rows * 4 + act_v,       # q,k,w,u,g in; o out (fused h + o)
     }
 
 
@@ -168,7 +169,10 @@ def run_chain(args, rank, world, device):
     c = CFG5
     B, T, H, K, V, W = c["B"], c["T"], c["H"], c["K"], c["V"], c["W"]
     xq, xk, xv, cw, cb, beta, gate = chain_inputs(B, T, H, K, V, W, 1234 + rank, device, torch.bfloat16)
-    layer = GatedDeltaNetForward(H, K, V, cw, cb)
+    layer = GatedDeltaNetForward(H, K, V, cw, cb, fused=not args.unfused)
+    fused = layer.uses_fused(torch.bfloat16)
+    names = (("causal_conv1d_x3", "recompute_w_u", "gated_delta_ho") if fused else
+             ("causal_conv1d_x3", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"))
     o = torch.empty(B, T, H, V, device=device, dtype=torch.bfloat16)
     stream = torch.cuda.current_stream()
 
@@ -186,6 +190,10 @@ def run_chain(args, rank, world, device):
         evs[1].record(stream)
         w, u = ops.recompute_w_u(bf["k"], bf["v"], beta, None, gate, a_mode=1, w=bf["w"], u=bf["u"])
         evs[2].record(stream)
+        if fused:
+            ops.gated_delta_fwd_ho(bf["q"], bf["k"], w, u, gate, layer.scale, o=o)
+            evs[3].record(stream)
+            return
         h, vn, _ = ops.chunk_fwd_h(bf["k"], u, gate, w=w, mode=1, h=bf["h"], v_new=bf["v"])
         evs[3].record(stream)
         ops.chunk_fwd_o(bf["q"], bf["k"], vn, gate, h, layer.scale, o=o)
@@ -200,7 +208,7 @@ def run_chain(args, rank, world, device):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)] for _ in range(args.steps)]
     t_wall0 = time.time()
     for i in range(args.steps):
         step(evs[i])
@@ -210,15 +218,15 @@ def run_chain(args, rank, world, device):
         dist.barrier()
     torch.cuda.synchronize()
     clocks = sampler.stop(t_wall0, t_wall1) if sampler else None
-    ms = evs[0][0].elapsed_time(evs[-1][4])
+    ms = evs[0][0].elapsed_time(evs[-1][len(names)])
     per = {n: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
-           for j, n in enumerate(("causal_conv1d_x3", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"))}
+           for j, n in enumerate(names)}
     from theorem_b200 import dist as D
     ms = D.max_over_ranks(ms, device=device)
     status = _lib.device_status()
     assert status == 0, f"in-kernel wait timed out (status {status})"
     return dict(ms=ms, per_op_ms=per, clocks=clocks, tokens_per_rank=B * T, layer=layer,
-                inputs=(xq, xk, xv, beta, gate), out=o)
+                inputs=(xq, xk, xv, beta, gate), out=o, launches_per_step=len(names) + 2, fused=fused)
 
 
 def run_e2e(args, device, layer, inputs):
@@ -452,6 +460,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-per-op", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--unfused", action="store_true",
+                    help="run chunk_fwd_h -> chunk_fwd_o as two kernels instead of the fused gated_delta_ho")
     ap.add_argument("--op", choices=["causal_conv1d", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o",
                                      "chunk_fwd_o_hf32", "causal_conv1d_bds"],
                     help="profiling mode: launch one op (bf16, chain settings) --iters times and exit")
@@ -499,30 +509,32 @@ def main(argv=None) -> int:
     value = world * res["tokens_per_rank"] / (ms / 1e3)
     by = chain_bytes(B, T, H, K, V, W)
     per_ms = res["per_op_ms"]
-    dom = max(("recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"), key=lambda n: per_ms[n])
-    if per_ms["causal_conv1d_x3"] / 3 > per_ms[dom]:
-        dom = "causal_conv1d"
-    dom_ms = per_ms["causal_conv1d_x3"] / 3 if dom == "causal_conv1d" else per_ms[dom]
+    per_launch = {("causal_conv1d" if n == "causal_conv1d_x3" else n): (v / 3 if n == "causal_conv1d_x3" else v)
+                  for n, v in per_ms.items()}
+    dom = max(per_launch, key=lambda n: per_launch[n])
+    dom_ms = per_launch[dom]
     achieved = by[dom] / (dom_ms * 1e-3) / 1e9
     traffic = None
     tf = ROOT / "profiles" / "dram_traffic.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(f"chain_{dom}")
     chain_step_bytes = 2 * by["causal_conv1d"] + (2 * B * T * H * V * 2 + H * V * (W + 1) * 4) + \
-        by["recompute_w_u"] + by["chunk_fwd_h"] + by["chunk_fwd_o"]
+        by["recompute_w_u"] + sum(by[n] for n in per_ms if n in ("chunk_fwd_h", "chunk_fwd_o", "gated_delta_ho"))
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD, **c, "D": H * K, "tokens_per_step_per_gpu": B * T,
                    "parallelism": f"dp{world} (each rank its own B=16 batch; no collective on the data path)",
-                   "l2": "inputs 1.6 GB per step per GPU > 126 MB L2 (no flush needed)"},
+                   "l2": "inputs 1.6 GB per step per GPU > 126 MB L2 (no flush needed)",
+                   "deltanet_kernels": ("recompute_w_u -> gated_delta_ho (chunk_fwd_h + chunk_fwd_o fused)"
+                                        if res["fused"] else "recompute_w_u -> chunk_fwd_h -> chunk_fwd_o")},
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": pk["hbm"], "unit": "GB/s",
                      "frac": achieved / pk["hbm"], "traffic": traffic, "peak_source": pk["src"],
                      "algorithmic_bytes_per_launch": by[dom], "avg_launch_ms": dom_ms},
         "chain": {"per_op_ms": per_ms, "algorithmic_bytes_per_step": chain_step_bytes,
                   "achieved_GB_s": chain_step_bytes / (ms * 1e-3) / 1e9},
-        "gpu_launches": 6 * args.steps,
+        "gpu_launches": res["launches_per_step"] * args.steps,
         "clocks": res["clocks"],
     }
     line.update(extra)

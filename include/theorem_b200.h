@@ -116,6 +116,25 @@ int thm_chunk_fwd_o_fwd(const void* q, const void* k, const void* v, const float
                         thm_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * gated_delta_fwd_ho -- chunk_fwd_h (mode 1) and chunk_fwd_o fused: the
+ * reference composes kernels/chunk_fwd_h/kernel.py:141-191 and
+ * kernels/chunk_fwd_o/kernel.py:146-212 through HBM (h and v_new written,
+ * then read back); this entry point produces the same o without either.
+ *
+ *   h_0 = h0 (or 0);  v_new_c = u_c - w_c h_c;
+ *   h_{c+1} = exp(g_last) h_c + (k_c * exp(g_last - g_c))^T v_new_c
+ *   o_c = scale * ( tril_{s<=t}((q k^T) * exp(g_t - g_s)) v_new_c + (q * exp(g)) h_c )
+ * q, k, w [B,T,H,K], u [B,T,H,V], o [B,T,H,V] in `dtype`; g [B,T,H] fp32;
+ * h0 (optional) and final_state (optional, = h_NT) [B,H,K,V] fp32.
+ * The state is carried in fp32; it is rounded to bf16 only as an MMA operand,
+ * and v_new once to bf16, as the separate ops do with a bf16 h.
+ * Built for dtype THM_BF16, K = V = 128, T % 64 == 0 (else THM_ERR_UNSUPPORTED).
+ * ------------------------------------------------------------------------- */
+int thm_gated_delta_fwd_ho(const void* q, const void* k, const void* w, const void* u, const float* g,
+                           const float* h0, void* o, float* final_state, float scale, int B, int T, int H, int K,
+                           int V, int dtype, thm_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Utilities
  * ------------------------------------------------------------------------- */
 /* Human-readable name of a thm_status. */

@@ -1,0 +1,118 @@
+"""GPU parity: the fused chunk_fwd_h + chunk_fwd_o kernel (gated_delta_fwd_ho)
+against the oracle (delta-rule recurrence then chunk_fwd_o) and against the two
+separate ops it replaces."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops as orc
+from tests.harness import assert_close
+from tests.synth import deltanet_inputs
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL = 2e-2  # bf16 activations, state rounded to bf16 as an MMA operand
+
+
+def _inputs(B, T, H, seed, K=128, V=128):
+    """q, k, w, u, g as the chain produces them (config 2 distributions), bf16."""
+    d = deltanet_inputs(B, T, H, K, V, seed)
+    q, k, v, beta, g = d["q"], d["k"], d["v"], d["beta"], d["g"]
+    A = orc.build_A(k.float(), beta, g, 1)
+    w, u = orc.recompute_w_u(k.float(), v.float(), beta, A, g)
+    w = torch.from_numpy(w).to(torch.bfloat16)
+    u = torch.from_numpy(u).to(torch.bfloat16)
+    gen = torch.Generator().manual_seed(seed + 1)
+    h0 = torch.randn(B, H, K, V, generator=gen) * (0.1 ** 0.5)
+    return q, k, w, u, g, h0
+
+
+def _oracle(q, k, w, u, g, h0, scale):
+    bf = lambda a: torch.from_numpy(np.asarray(a)).to(torch.bfloat16).double().numpy()  # noqa: E731
+    h, vn, fin = orc.chunk_fwd_h_delta(k.float(), w.float(), u.float(), g, h0)
+    o = orc.chunk_fwd_o(q.float(), k.float(), bf(vn), g, h, scale)
+    return o, fin
+
+
+def _dev(*ts):
+    return [None if t is None else t.to(DEV) for t in ts]
+
+
+@pytest.mark.parametrize("with_h0", [True, False])
+@pytest.mark.parametrize("T", [64, 192, 512])
+def test_fused_matches_oracle(with_h0, T):
+    from theorem_b200 import ops
+    B, H = 2, 3
+    q, k, w, u, g, h0 = _inputs(B, T, H, seed=T + with_h0)
+    h0 = h0 if with_h0 else None
+    scale = 128 ** -0.5
+    o, fin = ops.gated_delta_fwd_ho(*_dev(q, k, w, u, g), scale, h0=_dev(h0)[0], want_final=True)
+    ro, rfin = _oracle(q, k, w, u, g, h0, scale)
+    assert o.dtype == torch.bfloat16 and o.shape == (B, T, H, 128)
+    assert_close(o.float().cpu().double(), torch.from_numpy(ro), TOL, TOL, "o")
+    assert_close(fin.cpu().double(), torch.from_numpy(rfin), TOL, TOL, "final state")
+
+
+def test_fused_matches_separate_ops():
+    """Same roundings as chunk_fwd_h (bf16 h, v_new) -> chunk_fwd_o: near-identical o."""
+    from theorem_b200 import ops
+    B, T, H = 2, 1024, 4
+    q, k, w, u, g, h0 = (t.to(DEV) for t in _inputs(B, T, H, seed=77))
+    scale = 128 ** -0.5
+    o, fin = ops.gated_delta_fwd_ho(q, k, w, u, g, scale, h0=h0, want_final=True)
+    h, vn, fin2 = ops.chunk_fwd_h(k, u, g, w=w, h0=h0, mode=1, want_v_new=True, want_final=True,
+                                  h_dtype=torch.bfloat16)
+    o2 = ops.chunk_fwd_o(q, k, vn, g, h, scale)
+    d = (o.float() - o2.float()).abs()
+    assert float(d.max()) <= 1e-2 * float(o2.float().abs().max()) + 1e-3, float(d.max())
+    assert float(d.mean()) <= 1e-3 * float(o2.float().abs().mean()) + 1e-5, float(d.mean())
+    assert torch.allclose(fin, fin2, rtol=1e-4, atol=1e-5)
+
+
+def test_many_chunks_sampled():
+    """T = 4096 (64 chunks per sequence, every TMA stage and TMEM buffer reused),
+    B*H = 32 sequences, three checked against the oracle."""
+    from theorem_b200 import ops
+    B, T, H = 2, 4096, 16
+    q, k, w, u, g, h0 = _inputs(B, T, H, seed=5)
+    scale = 128 ** -0.5
+    o, fin = ops.gated_delta_fwd_ho(*_dev(q, k, w, u, g), scale, h0=_dev(h0)[0], want_final=True)
+    oc, fc = o.float().cpu(), fin.cpu()
+    assert torch.isfinite(oc).all() and torch.isfinite(fc).all()
+    for b, hh in [(0, 0), (1, 9), (1, 15)]:
+        sl = lambda t: t[b:b + 1, :, hh:hh + 1]  # noqa: E731
+        ro, rfin = _oracle(sl(q), sl(k), sl(w), sl(u), sl(g), h0[b:b + 1, hh:hh + 1], scale)
+        assert_close(oc[b:b + 1, :, hh:hh + 1].double(), torch.from_numpy(ro), TOL, TOL, f"o b={b} h={hh}")
+        assert_close(fc[b:b + 1, hh:hh + 1].double(), torch.from_numpy(rfin), TOL, TOL, f"final b={b} h={hh}")
+    o2, _ = ops.gated_delta_fwd_ho(*_dev(q, k, w, u, g), scale, h0=_dev(h0)[0])
+    assert torch.equal(o, o2), "repeated calls differ"
+
+
+def test_chain_fused_equals_unfused():
+    """The layer forward with the fused kernel against the same layer with
+    chunk_fwd_h -> chunk_fwd_o as separate launches."""
+    from theorem_b200.chain import GatedDeltaNetForward
+    B, T, H, K = 2, 512, 4, 128
+    D = H * K
+    gen = torch.Generator().manual_seed(3)
+    xs = [torch.randn(B, T, D, generator=gen).to(torch.bfloat16).to(DEV) for _ in range(3)]
+    cw = [(torch.randn(D, 4, generator=gen) * 0.5).to(DEV) for _ in range(3)]
+    cb = [(torch.randn(D, generator=gen) * 0.3).to(DEV) for _ in range(3)]
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=gen)).to(DEV)
+    inc = torch.nn.functional.logsigmoid(torch.randn(B, T, H, generator=gen)) / 16
+    g = inc.reshape(B, T // 64, 64, H).cumsum(2).reshape(B, T, H).contiguous().to(DEV)
+    fused = GatedDeltaNetForward(H, K, K, cw, cb)
+    sep = GatedDeltaNetForward(H, K, K, cw, cb, fused=False)
+    assert fused.uses_fused(torch.bfloat16) and not sep.uses_fused(torch.bfloat16)
+    o1, f1 = fused(*xs, beta, g)
+    o2, f2 = sep(*xs, beta, g)
+    assert_close(o1.float().cpu(), o2.float().cpu(), 1e-2, 1e-2, "o")
+    assert torch.allclose(f1, f2, rtol=1e-3, atol=1e-4)
+
+
+def test_unsupported_shapes_raise():
+    from theorem_b200 import ops
+    z = lambda *s: torch.zeros(*s, dtype=torch.bfloat16, device=DEV)  # noqa: E731
+    g = torch.zeros(1, 64, 1, device=DEV)
+    with pytest.raises(AssertionError):
+        ops.gated_delta_fwd_ho(z(1, 64, 1, 64), z(1, 64, 1, 64), z(1, 64, 1, 64), z(1, 64, 1, 64), g, 0.1)

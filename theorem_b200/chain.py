@@ -18,6 +18,11 @@ Inputs xq, xk, xv are channel-last [B, T, H*K] (bf16 or fp32); beta and g
 bf16 inputs -- the state is carried in fp32 inside chunk_fwd_h and only its
 stored per-chunk copy is rounded -- else fp32) are kept in buffers reused
 across calls with the same shape.
+
+With bf16 inputs and K = V = 128 the last two steps run as one kernel
+(ops.gated_delta_fwd_ho): the state recurrence and the output share a pass
+over the chunks and h, v_new never reach HBM. ``fused=False`` keeps the
+separate chunk_fwd_h -> chunk_fwd_o launches.
 """
 from __future__ import annotations
 
@@ -30,14 +35,18 @@ class GatedDeltaNetForward:
     """Callable layer forward; holds the depthwise conv weights [H*K, W] / [H*V, W]."""
 
     def __init__(self, H: int, K: int, V: int, conv_weights, conv_biases, activation: str = "silu",
-                 scale: float | None = None):
+                 scale: float | None = None, fused: bool = True):
         assert len(conv_weights) == 3 and len(conv_biases) == 3, "q, k, v conv weights and biases"
         self.H, self.K, self.V = H, K, V
         self.wq, self.wk, self.wv = (w.contiguous().float() for w in conv_weights)
         self.bq, self.bk, self.bv = (b.contiguous().float() for b in conv_biases)
         self.activation = activation
         self.scale = K ** -0.5 if scale is None else float(scale)
+        self.fused = fused
         self._buf: dict = {}
+
+    def uses_fused(self, dtype) -> bool:
+        return self.fused and dtype == torch.bfloat16 and self.K == 128 and self.V == 128
 
     def _buffers(self, xq, xv, B, T):
         key = (B, T, xq.dtype, xq.device)
@@ -51,8 +60,8 @@ class GatedDeltaNetForward:
                 v=torch.empty(B, T, H, V, device=dev, dtype=dt),
                 w=torch.empty(B, T, H, K, device=dev, dtype=dt),
                 u=torch.empty(B, T, H, V, device=dev, dtype=dt),
-                h=torch.empty(B, T // 64, H, K, V, device=dev,
-                              dtype=torch.bfloat16 if dt == torch.bfloat16 else torch.float32),
+                h=None if self.uses_fused(dt) else torch.empty(
+                    B, T // 64, H, K, V, device=dev, dtype=torch.bfloat16 if dt == torch.bfloat16 else torch.float32),
             )
         return self._buf
 
@@ -67,6 +76,8 @@ class GatedDeltaNetForward:
         ops.causal_conv1d(xk, self.wk, self.bk, self.activation, "bsd", K, out=k.view(B, T, H * K))
         ops.causal_conv1d(xv, self.wv, self.bv, self.activation, "bsd", 0, out=v.view(B, T, H * V))
         w, u = ops.recompute_w_u(k, v, beta, None, g, a_mode=1, w=bf["w"], u=bf["u"])
+        if self.uses_fused(xq.dtype):
+            return ops.gated_delta_fwd_ho(q, k, w, u, g, self.scale, h0=h0, want_final=final_state, o=out)
         h, v_new, fin = ops.chunk_fwd_h(k, u, g, w=w, h0=h0, mode=1, want_v_new=True, want_final=final_state,
                                         h=bf["h"], v_new=v)
         o = ops.chunk_fwd_o(q, k, v_new, g, h, self.scale, o=out)

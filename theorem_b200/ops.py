@@ -148,3 +148,31 @@ def chunk_fwd_o(q, k, v, g, h, scale: float, o=None):
                                          float(scale), B, T, H, K, V, L.dtype_code(q), L.dtype_code(h), st),
             "thm_chunk_fwd_o_fwd")
     return o
+
+
+def gated_delta_fwd_ho(q, k, w, u, g, scale: float, h0=None, want_final: bool = False, o=None):
+    """chunk_fwd_h (delta rule) and chunk_fwd_o fused in one kernel: returns
+    (o, final state or None). Same result as
+    ``chunk_fwd_h(k, u, g, w=w, h0=h0, mode=1, want_v_new=True, h_dtype=bf16)``
+    followed by ``chunk_fwd_o(q, k, v_new, g, h, scale)``, without writing h or
+    v_new (kernels/chunk_fwd_h/kernel.py:141-191 + kernels/chunk_fwd_o/kernel.py:146-212).
+    Built for bf16, K = V = 128."""
+    _cuda(q, k, w, u, g, h0)
+    _contig(q, k, w, u, g, h0)
+    B, T, H, K = q.shape
+    V = u.shape[-1]
+    assert k.shape == q.shape and w.shape == q.shape and u.shape == (B, T, H, V)
+    assert k.dtype == q.dtype and w.dtype == q.dtype and u.dtype == q.dtype
+    assert g.shape == (B, T, H) and g.dtype == torch.float32
+    assert T % BT == 0, f"T={T} must be divisible by BT={BT}"
+    if h0 is not None:
+        assert h0.shape == (B, H, K, V) and h0.dtype == torch.float32
+    if o is None:
+        o = torch.empty(B, T, H, V, dtype=q.dtype, device=q.device)
+    assert o.shape == (B, T, H, V) and o.dtype == q.dtype and o.is_contiguous()
+    final = torch.empty(B, H, K, V, device=q.device, dtype=torch.float32) if want_final else None
+    st = L.stream_of(q)
+    L.check(L.load().thm_gated_delta_fwd_ho(L.ptr(q), L.ptr(k), L.ptr(w), L.ptr(u), L.ptr(g), L.ptr(h0), L.ptr(o),
+                                            L.ptr(final), float(scale), B, T, H, K, V, L.dtype_code(q), st),
+            "thm_gated_delta_fwd_ho")
+    return o, final
