@@ -82,11 +82,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::OFF_MISC + 1024);
   uint64_t* full = bars;          // [2] TMA stage landed
   uint64_t* s_ready = bars + 2;   // h_c copied to smem (math threads)
-  uint64_t* vn_ready = bars + 3;  // P and v_new in smem (math threads)
-  uint64_t* bar_s = bars + 4;     // S = q k^T in TMEM
-  uint64_t* bar_a = bars + 5;     // X, G in TMEM
-  uint64_t* bar_b = bars + 6;     // U, L in TMEM (stage consumed)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  uint64_t* vn_ready = bars + 3;  // v_new in smem (math threads)
+  uint64_t* p_ready = bars + 4;   // P in smem (math threads)
+  uint64_t* bar_s = bars + 5;     // S = q k^T in TMEM
+  uint64_t* bar_a = bars + 6;     // X, G in TMEM
+  uint64_t* bar_u = bars + 7;     // U in TMEM (stage consumed)
+  uint64_t* bar_l = bars + 8;     // L in TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x;
@@ -111,9 +113,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&full[1], 1);
     mbar_init(s_ready, kMath);
     mbar_init(vn_ready, kMath);
+    mbar_init(p_ready, kMath);
     mbar_init(bar_s, 1);
     mbar_init(bar_a, 1);
-    mbar_init(bar_b, 1);
+    mbar_init(bar_u, 1);
+    mbar_init(bar_l, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -133,17 +137,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kMath / 32) {
     // ---------------- TMA + tcgen05 issuer (one thread) ----------------
     if (lane == 0) {
-      issue_tma(0, 0);
-      if (NT > 1) issue_tma(1, 1);
-      int pend_b = -1;  // parity of the last U/L commit not yet waited for
-      for (int c = 0; c < NT && ok; ++c) {
-        const int st = c & 1;
-        const uint32_t ph = c & 1;
-        const uint32_t stg = sbase + st * Ly::STAGE;
-        const uint32_t tXG = tbase + 128 + 128 * st;
-        // S = q k^T (tS was read by P(c-1) before vn_ready(c-1))
-        if (!mbar_wait(&full[st], (c >> 1) & 1, &g_status_ho)) { ok = false; break; }
-        tc_fence_after();
+      // Order per chunk c: X, G (state path) | U (state path) | L | S of chunk c+1
+      // (off the state path: S and its P are ready before X, G of the next chunk).
+      auto issue_s = [&](int c) {
+        const uint32_t stg = sbase + (c & 1) * Ly::STAGE;
 #pragma unroll
         for (int kq = 0; kq < kK / 16; ++kq) {
           const uint32_t off = (kq / 4) * 8192 + (kq % 4) * 32;
@@ -151,6 +148,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                       kIdS, kq > 0);
         }
         mma_commit(bar_s);
+      };
+      uint64_t* last_bar = nullptr;  // last commit, waited (bounded) before TMEM is released
+      uint32_t last_ph = 0;
+      issue_tma(0, 0);
+      if (NT > 1) issue_tma(1, 1);
+      if (mbar_wait(&full[0], 0, &g_status_ho)) {
+        tc_fence_after();
+        issue_s(0);
+        last_bar = bar_s;
+      } else {
+        ok = false;
+      }
+      for (int c = 0; c < NT && ok; ++c) {
+        const int st = c & 1;
+        const uint32_t ph = c & 1;
+        const uint32_t stg = sbase + st * Ly::STAGE;
+        const uint32_t tXG = tbase + 128 + 128 * st;
         // X = w h_c, G = q h_c
         if (!mbar_wait(s_ready, ph, &g_status_ho)) { ok = false; break; }
         tc_fence_after();
@@ -162,28 +176,40 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_bf16_ss(tXG + (16u << 16), make_sdesc(stg + Ly::OFF_Q + off, 16, 1024), hd, kIdXG, kq > 0);
         }
         mma_commit(bar_a);
-        // U = k^T (v_new e^{g_last - g_t}), L = P v_new
+        last_bar = bar_a, last_ph = ph;
+        // U = k^T (v_new e^{g_last - g_t})
         if (!mbar_wait(vn_ready, ph, &g_status_ho)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int q = 0; q < kBT / 16; ++q)
           mma_bf16_ss(tU, make_sdesc(stg + Ly::OFF_K + q * 2048, 8192, 1024),
                       make_sdesc(stg + Ly::OFF_U + q * 2048, 8192, 1024), kIdU, q > 0);
+        mma_commit(bar_u);
+        last_bar = bar_u;
+        // L = P v_new
+        if (!mbar_wait(p_ready, ph, &g_status_ho)) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll
         for (int q = 0; q < kBT / 16; ++q)
           mma_bf16_ss(tL, make_sdesc(sbase + Ly::OFF_P + q * 32, 16, 1024),
                       make_sdesc(sbase + Ly::OFF_VN + q * 2048, 8192, 1024), kIdL, q > 0);
-        mma_commit(bar_b);
-        pend_b = (int)ph;
+        mma_commit(bar_l);
+        last_bar = bar_l;
+        // S of chunk c+1 (tS was read by P(c) before p_ready(c))
+        if (c + 1 < NT) {
+          if (!mbar_wait(&full[st ^ 1], ((c + 1) >> 1) & 1, &g_status_ho)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(c + 1);
+          last_bar = bar_s, last_ph = (c + 1) & 1;
+        }
         // Stage st is free once U has read it: prefetch chunk c+2.
         if (c + 2 < NT) {
-          if (!mbar_wait(bar_b, ph, &g_status_ho)) { ok = false; break; }
-          pend_b = -1;
+          if (!mbar_wait(bar_u, ph, &g_status_ho)) { ok = false; break; }
           issue_tma(c + 2, st);
         }
       }
-      // Before TMEM is released: the last commits have landed (bounded).
-      if (pend_b >= 0) mbar_wait(bar_b, (uint32_t)pend_b, &g_status_ho);
+      // Commits complete in issue order: the last one covers every MMA issued.
+      if (last_bar != nullptr) mbar_wait(last_bar, last_ph, &g_status_ho);
     }
   } else {
     // ---------------- math warps (256 threads) ----------------
@@ -263,21 +289,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(s_ready);
 
-      // (2) epilogue of chunk c-1 while the tensor core computes S, X, G of chunk c
-      cp_async_wait<1>();  // this chunk's gates have landed (visible after the next barrier)
+      // (2) epilogue of chunk c-1 while the tensor core computes X, G of chunk c
+      cp_async_wait<0>();  // this chunk's gates have landed (visible after the next barrier)
       if (c > 0) {
+        ok = mbar_wait(bar_l, (c - 1) & 1, &g_status_ho) && ok;
         if (!epilogue(c - 1, ok)) { ok = false; break; }
       } else if (!named_bar_and(1, kMath, ok)) {
         ok = false;
         break;
       }
+      // Gates of chunk c+1 into sG[st^1]: every thread is past P(c-1), its last reader.
+      if (c >= 1 && c + 1 < NT && tid < kBT)
+        cp_async4(&sG[(st ^ 1) * 64 + tid], g + (long long)(b * T_len + (c + 1) * kBT + tid) * H + hh);
+      cp_async_commit();
       const float gl = gc[kBT - 1];
+      const float g0 = gc[r0], g1 = gc[r1];
       if (tid < kBT) sEg[st * 64 + tid] = __expf(gc[tid]) * scale;
 
-      // (3) P = tril(S e^{g_t - g_s}) -> smem (this warpgroup: 32 columns)
+      // (3) P = tril(S e^{g_t - g_s}) -> smem (this warpgroup: 32 columns), while X, G run
       ok = mbar_wait(bar_s, ph, &g_status_ho) && ok;
       tc_fence_after();
-      const float g0 = gc[r0], g1 = gc[r1];
       {
         float sv[16];
         tmem_ld_16x256b_x4(tS + lane_row + 32 * half, sv);
@@ -294,6 +325,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint32_t*>(pb + sw128_offset(r1, cc, kBT, 2)) = pack_bf16x2(p10, p11);
         }
       }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_ready);
 
       // (4) v_new = u - X -> smem (this warpgroup: 64 columns)
       ok = mbar_wait(bar_a, ph, &g_status_ho) && ok;
@@ -323,12 +357,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(vn_ready);
 
-      // (5) h_{c+1} = e^{g_last} h_c + U; gates of chunk c+2 (stage st's TMA is the issuer's)
-      ok = mbar_wait(bar_b, ph, &g_status_ho) && ok;
+      // (5) h_{c+1} = e^{g_last} h_c + U
+      ok = mbar_wait(bar_u, ph, &g_status_ho) && ok;
       tc_fence_after();
-      if (c + 2 < NT && tid < kBT)
-        cp_async4(&sG[st * 64 + tid], g + (long long)(b * T_len + (c + 2) * kBT + tid) * H + hh);
-      cp_async_commit();
       {
         const float eg = __expf(gl);
 #pragma unroll
@@ -341,6 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
     }
+    if (ok && NT > 0) ok = mbar_wait(bar_l, (NT - 1) & 1, &g_status_ho);
     if (ok && NT > 0) ok = epilogue(NT - 1, ok);
     cp_async_wait<0>();
     if (tid == 0) bulk_wait_group0();
