@@ -38,11 +38,22 @@ THM_DEFINE_STATUS(g_status_ho)
 namespace thm {
 namespace delta_ho {
 
-constexpr int kMath = 256;             // 8 math warps
-constexpr int kThreads = kMath + 32;   // + one TMA / tcgen05 issuer warp
 constexpr int kBT = 64;
 constexpr int kK = 128;
 constexpr int kV = 128;
+constexpr int kMath = 256;             // math warps: 2 warpgroups
+constexpr int kThreads = kMath + 64;   // + tcgen05 issuer warp + TMA producer warp
+constexpr int kWG = kMath / 128;       // warps sharing a TMEM subpartition
+constexpr int kCW = kV / kWG;          // V columns per math warp
+constexpr int kPW = kBT / kWG;         // P columns per math warp
+
+// 16x256b TMEM load of N/2 8-column groups (N = 2, 4 or 8 registers per group pair).
+template <int N>
+__device__ __forceinline__ void tmem_ld_16x256b(uint32_t taddr, float* v) {
+  if constexpr (N == 8) tmem_ld_16x256b_x8(taddr, v);
+  else if constexpr (N == 4) tmem_ld_16x256b_x4(taddr, v);
+  else tmem_ld_16x256b_x2(taddr, v);
+}
 
 struct Layout {
   static constexpr int TILE = kBT * 128 * 2;  // [64 x 128] bf16 = two 8 KB boxes
@@ -81,9 +92,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* sEg = reinterpret_cast<float*>(sm + Ly::OFF_MISC + 512);    // [2][64] scale e^{g_t}
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::OFF_MISC + 1024);
   uint64_t* full = bars;          // [2] TMA stage landed
-  uint64_t* s_ready = bars + 2;   // h_c copied to smem (math threads)
-  uint64_t* vn_ready = bars + 3;  // v_new in smem (math threads)
-  uint64_t* p_ready = bars + 4;   // P in smem (math threads)
+  uint64_t* s_ready = bars + 2;   // h_c copied to smem (one arrival per math warp)
+  uint64_t* vn_ready = bars + 3;  // v_new in smem (one arrival per math warp)
+  uint64_t* p_ready = bars + 4;   // P in smem (one arrival per math warp)
   uint64_t* bar_s = bars + 5;     // S = q k^T in TMEM
   uint64_t* bar_a = bars + 6;     // X, G in TMEM
   uint64_t* bar_u = bars + 7;     // U in TMEM (stage consumed)
@@ -95,25 +106,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b = bh / H, hh = bh - (bh / H) * H;
   const int NT = T_len / kBT;
 
-  auto issue_tma = [&](int c, int st) {
-    uint8_t* base = sm + st * Ly::STAGE;
-    const int row0 = b * T_len + c * kBT;
-    mbar_arrive_expect_tx(&full[st], Ly::STAGE);
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      tma_load_3d(base + Ly::OFF_K + j * 8192, &tm_k, &full[st], j * 64, hh, row0);
-      tma_load_3d(base + Ly::OFF_Q + j * 8192, &tm_q, &full[st], j * 64, hh, row0);
-      tma_load_3d(base + Ly::OFF_W + j * 8192, &tm_w, &full[st], j * 64, hh, row0);
-      tma_load_3d(base + Ly::OFF_U + j * 8192, &tm_u, &full[st], j * 64, hh, row0);
-    }
-  };
-
   if (tid == 0) {
     mbar_init(&full[0], 1);
     mbar_init(&full[1], 1);
-    mbar_init(s_ready, kMath);
-    mbar_init(vn_ready, kMath);
-    mbar_init(p_ready, kMath);
+    mbar_init(s_ready, kMath / 32);
+    mbar_init(vn_ready, kMath / 32);
+    mbar_init(p_ready, kMath / 32);
     mbar_init(bar_s, 1);
     mbar_init(bar_a, 1);
     mbar_init(bar_u, 1);
@@ -134,11 +132,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tU = tbase, tL = tbase + 384, tS = tbase + 384 + (16u << 16);
   bool ok = true;
 
-  if (warp == kMath / 32) {
-    // ---------------- TMA + tcgen05 issuer (one thread) ----------------
+  if (warp == kMath / 32 + 1) {
+    // ---------------- TMA producer (one thread) ----------------
     if (lane == 0) {
-      // Order per chunk c: X, G (state path) | U (state path) | L | S of chunk c+1
-      // (off the state path: S and its P are ready before X, G of the next chunk).
+      auto issue_tma = [&](int c) {
+        const int st = c & 1;
+        uint8_t* base = sm + st * Ly::STAGE;
+        const int row0 = b * T_len + c * kBT;
+        mbar_arrive_expect_tx(&full[st], Ly::STAGE);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          tma_load_3d(base + Ly::OFF_K + j * 8192, &tm_k, &full[st], j * 64, hh, row0);
+          tma_load_3d(base + Ly::OFF_Q + j * 8192, &tm_q, &full[st], j * 64, hh, row0);
+          tma_load_3d(base + Ly::OFF_W + j * 8192, &tm_w, &full[st], j * 64, hh, row0);
+          tma_load_3d(base + Ly::OFF_U + j * 8192, &tm_u, &full[st], j * 64, hh, row0);
+        }
+      };
+      issue_tma(0);
+      if (NT > 1) issue_tma(1);
+      int issued = NT > 1 ? 2 : 1;
+      // Stage c & 1 is free once U(c) has read it.
+      for (int c = 0; c + 2 < NT; ++c) {
+        if (!mbar_wait(bar_u, c & 1, &g_status_ho)) { ok = false; break; }
+        issue_tma(c + 2);
+        issued = c + 3;
+      }
+      // No TMA may be in flight when the CTA exits: the last loads have landed (bounded).
+      for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j) mbar_wait(&full[j & 1], (j >> 1) & 1, &g_status_ho);
+    }
+  } else if (warp == kMath / 32) {
+    // ---------------- tcgen05 issuer (one thread) ----------------
+    // Per chunk c: X, G | S of chunk c+1 (once P(c) has read S(c)) | U | L.
+    if (lane == 0) {
       auto issue_s = [&](int c) {
         const uint32_t stg = sbase + (c & 1) * Ly::STAGE;
 #pragma unroll
@@ -151,8 +176,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       uint64_t* last_bar = nullptr;  // last commit, waited (bounded) before TMEM is released
       uint32_t last_ph = 0;
-      issue_tma(0, 0);
-      if (NT > 1) issue_tma(1, 1);
       if (mbar_wait(&full[0], 0, &g_status_ho)) {
         tc_fence_after();
         issue_s(0);
@@ -165,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = c & 1;
         const uint32_t stg = sbase + st * Ly::STAGE;
         const uint32_t tXG = tbase + 128 + 128 * st;
-        // X = w h_c, G = q h_c
+        // X = w h_c, G = q h_c (stage c landed: S(c) was issued after its full wait)
         if (!mbar_wait(s_ready, ph, &g_status_ho)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -177,7 +200,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(bar_a);
         last_bar = bar_a, last_ph = ph;
-        // U = k^T (v_new e^{g_last - g_t})
+        // S of chunk c+1 while the math warps form v_new(c): tS is free once P(c) is in smem.
+        if (!mbar_wait(p_ready, ph, &g_status_ho)) { ok = false; break; }
+        if (c + 1 < NT) {
+          if (!mbar_wait(&full[st ^ 1], ((c + 1) >> 1) & 1, &g_status_ho)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(c + 1);
+          last_bar = bar_s, last_ph = (c + 1) & 1;
+        }
+        // U = k^T (v_new e^{g_last - g_t}), then L = P v_new
         if (!mbar_wait(vn_ready, ph, &g_status_ho)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -185,54 +216,42 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_bf16_ss(tU, make_sdesc(stg + Ly::OFF_K + q * 2048, 8192, 1024),
                       make_sdesc(stg + Ly::OFF_U + q * 2048, 8192, 1024), kIdU, q > 0);
         mma_commit(bar_u);
-        last_bar = bar_u;
-        // L = P v_new
-        if (!mbar_wait(p_ready, ph, &g_status_ho)) { ok = false; break; }
-        tc_fence_after();
 #pragma unroll
         for (int q = 0; q < kBT / 16; ++q)
           mma_bf16_ss(tL, make_sdesc(sbase + Ly::OFF_P + q * 32, 16, 1024),
                       make_sdesc(sbase + Ly::OFF_VN + q * 2048, 8192, 1024), kIdL, q > 0);
         mma_commit(bar_l);
-        last_bar = bar_l;
-        // S of chunk c+1 (tS was read by P(c) before p_ready(c))
-        if (c + 1 < NT) {
-          if (!mbar_wait(&full[st ^ 1], ((c + 1) >> 1) & 1, &g_status_ho)) { ok = false; break; }
-          tc_fence_after();
-          issue_s(c + 1);
-          last_bar = bar_s, last_ph = (c + 1) & 1;
-        }
-        // Stage st is free once U has read it: prefetch chunk c+2.
-        if (c + 2 < NT) {
-          if (!mbar_wait(bar_u, ph, &g_status_ho)) { ok = false; break; }
-          issue_tma(c + 2, st);
-        }
+        last_bar = bar_l, last_ph = ph;
       }
       // Commits complete in issue order: the last one covers every MMA issued.
       if (last_bar != nullptr) mbar_wait(last_bar, last_ph, &g_status_ho);
     }
   } else {
-    // ---------------- math warps (256 threads) ----------------
-    const int sp = warp & 3;      // TMEM subpartition of this warp
-    const int half = warp >> 2;   // 64-column half of V this warpgroup owns
-    const int kk = tid & 127;     // state row (d) of this thread
+    // ---------------- math warps ----------------
+    // Warp w reads TMEM lanes 32 (w % 4) ..; the kWG warps of a subpartition
+    // split the 128 V columns (and the 64 P columns) between them.
+    const int sp = warp & 3;
+    const int qc = kCW * (warp >> 2);  // first V column of this warp
+    const int pc = kPW * (warp >> 2);  // first P column of this warp
+    const int kk = tid & 127;          // state row (d) of this thread
     const uint32_t lane_row = (uint32_t)(32 * sp) << 16;
     const int r0 = 16 * sp + (lane >> 2), r1 = r0 + 8;  // 16x256b rows of M=64 accumulators
+    const int c4 = 2 * (lane & 3);
 
-    float S[64];
+    float S[kCW];
 #pragma unroll
-    for (int j = 0; j < 64; ++j) S[j] = 0.f;
+    for (int j = 0; j < kCW; ++j) S[j] = 0.f;
     if (h0 != nullptr) {
-      const float* src = h0 + (((long long)b * H + hh) * kK + kk) * kV + 64 * half;
+      const float* src = h0 + (((long long)b * H + hh) * kK + kk) * kV + qc;
 #pragma unroll
-      for (int j = 0; j < 64; j += 4) {
+      for (int j = 0; j < kCW; j += 4) {
         const float4 x = *reinterpret_cast<const float4*>(src + j);
         S[j] = x.x; S[j + 1] = x.y; S[j + 2] = x.z; S[j + 3] = x.w;
       }
     }
 
     // o tile of chunk j: scale L + scale e^{g_t} G -> staging -> TMA store.
-    // The two named barriers also serve as the uniform timeout vote.
+    // Its first named barrier is also the uniform timeout vote.
     auto epilogue = [&](int j, bool good) -> bool {
       if (tid == 0) bulk_wait_group_read0();  // the previous o tile has left the staging buffer
       if (!named_bar_and(1, kMath, good)) return false;
@@ -240,13 +259,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float e0 = sEg[(j & 1) * 64 + r0], e1 = sEg[(j & 1) * 64 + r1];
       uint8_t* ob = sm + Ly::OFF_O;
 #pragma unroll
-      for (int hq = 0; hq < 2; ++hq) {  // 32 columns at a time (register pressure)
+      for (int hq = 0; hq < kCW / 32; ++hq) {  // 32 columns at a time (register pressure)
         float lv[16], gv[16];
-        tmem_ld_16x256b_x4(tL + lane_row + 64 * half + 32 * hq, lv);
-        tmem_ld_16x256b_x4(tbase + 128 + 128 * (j & 1) + lane_row + (16u << 16) + 64 * half + 32 * hq, gv);
+        tmem_ld_16x256b_x4(tL + lane_row + qc + 32 * hq, lv);
+        tmem_ld_16x256b_x4(tbase + 128 + 128 * (j & 1) + lane_row + (16u << 16) + qc + 32 * hq, gv);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const int cc = 64 * half + 32 * hq + 8 * q + 2 * (lane & 3);
+          const int cc = qc + 32 * hq + 8 * q + c4;
           *reinterpret_cast<uint32_t*>(ob + sw128_offset(r0, cc, kBT, 2)) =
               pack_bf16x2(fmaf(lv[4 * q], scale, gv[4 * q] * e0), fmaf(lv[4 * q + 1], scale, gv[4 * q + 1] * e0));
           *reinterpret_cast<uint32_t*>(ob + sw128_offset(r1, cc, kBT, 2)) =
@@ -274,20 +293,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // (1) h_c -> shared memory (bf16, MN-major B operand of X and G)
       {
-        uint8_t* tile = sm + Ly::OFF_S + half * (kK * 128);
+        uint8_t* tile = sm + Ly::OFF_S + (qc >> 6) * (kK * 128);
 #pragma unroll
-        for (int j = 0; j < 64; j += 8) {
+        for (int j = 0; j < kCW; j += 8) {
           uint4 p;
           p.x = pack_bf16x2(S[j], S[j + 1]);
           p.y = pack_bf16x2(S[j + 2], S[j + 3]);
           p.z = pack_bf16x2(S[j + 4], S[j + 5]);
           p.w = pack_bf16x2(S[j + 6], S[j + 7]);
-          *reinterpret_cast<uint4*>(tile + sw128_offset(kk, j, kK, 2)) = p;
+          *reinterpret_cast<uint4*>(tile + sw128_offset(kk, (qc & 63) + j, kK, 2)) = p;
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(s_ready);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_ready);  // one arrival per warp
 
       // (2) epilogue of chunk c-1 while the tensor core computes X, G of chunk c
       cp_async_wait<0>();  // this chunk's gates have landed (visible after the next barrier)
@@ -298,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
-      // Gates of chunk c+1 into sG[st^1]: every thread is past P(c-1), its last reader.
+      // Gates of chunk c+1 into sG[st^1]: every thread is past chunk c-1, its last reader.
       if (c >= 1 && c + 1 < NT && tid < kBT)
         cp_async4(&sG[(st ^ 1) * 64 + tid], g + (long long)(b * T_len + (c + 1) * kBT + tid) * H + hh);
       cp_async_commit();
@@ -306,16 +326,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float g0 = gc[r0], g1 = gc[r1];
       if (tid < kBT) sEg[st * 64 + tid] = __expf(gc[tid]) * scale;
 
-      // (3) P = tril(S e^{g_t - g_s}) -> smem (this warpgroup: 32 columns), while X, G run
+      // (3) P = tril(S e^{g_t - g_s}) -> smem (this warp: kPW columns), while X, G run
       ok = mbar_wait(bar_s, ph, &g_status_ho) && ok;
       tc_fence_after();
       {
-        float sv[16];
-        tmem_ld_16x256b_x4(tS + lane_row + 32 * half, sv);
+        float sv[kPW / 2];
+        tmem_ld_16x256b<kPW / 4>(tS + lane_row + pc, sv);
         uint8_t* pb = sm + Ly::OFF_P;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int cc = 32 * half + 8 * q + 2 * (lane & 3);
+        for (int q = 0; q < kPW / 8; ++q) {
+          const int cc = pc + 8 * q + c4;
           const float gc0 = gc[cc], gc1 = gc[cc + 1];
           const float p00 = (cc <= r0) ? sv[4 * q] * __expf(g0 - gc0) : 0.f;
           const float p01 = (cc + 1 <= r0) ? sv[4 * q + 1] * __expf(g0 - gc1) : 0.f;
@@ -327,20 +347,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_ready);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);  // one arrival per warp
 
-      // (4) v_new = u - X -> smem (this warpgroup: 64 columns)
+      // (4) v_new = u - X -> smem (this warp: kCW columns)
       ok = mbar_wait(bar_a, ph, &g_status_ho) && ok;
       tc_fence_after();
       {
-        float xv[32];
-        tmem_ld_16x256b_x8(tXG + lane_row + 64 * half, xv);
+        float xv[kCW / 2];
+        tmem_ld_16x256b<kCW / 8>(tXG + lane_row + qc, xv);
         const float d0 = __expf(gl - g0), d1 = __expf(gl - g1);
         uint8_t* ut = stage + Ly::OFF_U;
         uint8_t* vn = sm + Ly::OFF_VN;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int cc = 64 * half + 8 * q + 2 * (lane & 3);
+        for (int q = 0; q < kCW / 8; ++q) {
+          const int cc = qc + 8 * q + c4;
           const uint32_t o0 = sw128_offset(r0, cc, kBT, 2), o1 = sw128_offset(r1, cc, kBT, 2);
           const float2 u0 = bf2_to_f2(ld_u32(ut + o0)), u1 = bf2_to_f2(ld_u32(ut + o1));
           const float n00 = u0.x - xv[4 * q], n01 = u0.y - xv[4 * q + 1];
@@ -355,7 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(vn_ready);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(vn_ready);  // one arrival per warp
 
       // (5) h_{c+1} = e^{g_last} h_c + U
       ok = mbar_wait(bar_u, ph, &g_status_ho) && ok;
@@ -363,9 +385,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         const float eg = __expf(gl);
 #pragma unroll
-        for (int hq = 0; hq < 2; ++hq) {
+        for (int hq = 0; hq < kCW / 32; ++hq) {
           float ur[32];
-          tmem_ld32(tU + lane_row + 64 * half + 32 * hq, ur);
+          tmem_ld32(tU + lane_row + qc + 32 * hq, ur);
 #pragma unroll
           for (int j = 0; j < 32; ++j) S[32 * hq + j] = fmaf(eg, S[32 * hq + j], ur[j]);
         }
@@ -377,9 +399,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     cp_async_wait<0>();
     if (tid == 0) bulk_wait_group0();
     if (ok && final_state != nullptr) {
-      float* dst = final_state + (((long long)b * H + hh) * kK + kk) * kV + 64 * half;
+      float* dst = final_state + (((long long)b * H + hh) * kK + kk) * kV + qc;
 #pragma unroll
-      for (int j = 0; j < 64; j += 4)
+      for (int j = 0; j < kCW; j += 4)
         *reinterpret_cast<float4*>(dst + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
     }
   }

@@ -337,6 +337,19 @@ __device__ __forceinline__ void tmem_ld_16x256b_x8(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Same shape, 2 repetitions (16 columns): v[4j..4j+3] as above for j < 2.
+__device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Same shape, 4 repetitions (32 columns): v[4j..4j+3] as above for j < 4.
 __device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, float* v) {
   uint32_t r[16];
