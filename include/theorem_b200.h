@@ -79,6 +79,32 @@ int thm_recompute_w_u_fwd(const void* k, const void* v, const float* beta, const
                           int a_mode, thm_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * build_A -- the upstream producer of recompute_w_u's A
+ * (kernels/recompute_w_u/reference.py:48-91, `_build_A`), for callers that
+ * pass A to thm_recompute_w_u_fwd with a_mode 0.
+ *
+ *   A_c = (I + sign * M_c)^-1,  M_c = strict_tril(beta_i k_i.k_j exp(g_i - g_j))
+ * per 64-token chunk c; sign = -1 is the reference (I - M)^-1, +1 gated
+ * DeltaNet's (I + M)^-1. k [B,T,H,K] in `dtype`; beta, g [B,T,H] fp32;
+ * A [B,T,H,64] fp32 (row t of its chunk's matrix at position t).
+ * T % 64 == 0; K in {64, 128}.
+ * ------------------------------------------------------------------------- */
+int thm_build_A_fwd(const void* k, const float* beta, const float* g, float* A, int B, int T, int H, int K,
+                    int dtype, int sign, thm_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * chunk_local_cumsum -- the upstream producer of g: the reference's
+ * generators form g as a per-chunk cumulative sum of per-token log-decay
+ * increments (kernels/chunk_fwd_h/reference.py:41-45,
+ * kernels/recompute_w_u/reference.py:103-106).
+ *
+ *   g[b, c*64 + i, h] = scale * sum_{j <= i} g_inc[b, c*64 + j, h]
+ * g_inc, g [B,T,H] fp32 (g may be g_inc: in place); T % 64 == 0.
+ * ------------------------------------------------------------------------- */
+int thm_chunk_local_cumsum_fwd(const float* g_inc, float* g, int B, int T, int H, float scale,
+                               thm_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * chunk_fwd_h -- replaces kernels/chunk_fwd_h/kernel.py:141-191
  * (custom_kernel; Triton chunk_fwd_h_kernel :61-138).
  *

@@ -13,7 +13,7 @@ HEADER = Path(__file__).resolve().parent.parent / "include" / "theorem_b200.h"
 def declared_symbols():
     text = HEADER.read_text()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(thm_[a-z0-9_]+)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(thm_[A-Za-z0-9_]+)\s*\(", text)))
 
 
 def test_library_is_built():

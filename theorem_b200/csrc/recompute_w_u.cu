@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b = bh / H, h = bh - (bh / H) * H;
   const int row0 = b * T_len + c * kBT;
   const bool fused = a_mode != 0;
+  const bool a_only = w == nullptr;  // build_A: A (a_out) is the only output, no v tile
   uint32_t mma_phase = 0;
   int pending = -1;  // parity of an MMA commit not yet waited for (cleanup path)
 
@@ -107,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     constexpr int kBox = 128 / Ly::ES;
-    uint32_t bytes = Ly::K_BYTES + Ly::V_BYTES + (fused ? Ly::KK_BYTES : Ly::AF_BYTES);
+    uint32_t bytes = Ly::K_BYTES + (a_only ? 0u : (uint32_t)Ly::V_BYTES) + (fused ? Ly::KK_BYTES : Ly::AF_BYTES);
     mbar_arrive_expect_tx(bar_tma, bytes);
 #pragma unroll
     for (int j = 0; j < K / kBox; ++j) {
@@ -115,7 +116,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!kBf16 && fused) tma_load_3d(sm + Ly::OFF_KK + j * kBT * 128, &tm_kk, bar_tma, j * kBox, h, row0);
     }
 #pragma unroll
-    for (int j = 0; j < V / kBox; ++j) tma_load_3d(sm + Ly::OFF_V + j * kBT * 128, &tm_v, bar_tma, j * kBox, h, row0);
+    for (int j = 0; j < V / kBox; ++j)
+      if (!a_only) tma_load_3d(sm + Ly::OFF_V + j * kBT * 128, &tm_v, bar_tma, j * kBox, h, row0);
     if (!fused) {
       tma_load_3d(sm + Ly::OFF_AF, &tm_a, bar_tma, 0, h, row0);
       tma_load_3d(sm + Ly::OFF_AF + kBT * 128, &tm_a, bar_tma, 32, h, row0);
@@ -224,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < kBT; ++i) a_out[((long long)(row0 + i) * H + h) * kBT + j] = x[i];
     }
-  } else if (!fused || tid >= kBT) {
+  } else if (!a_only && (!fused || tid >= kBT)) {
     const int t0 = fused ? tid - kBT : tid;
     const int nt = fused ? kThreads - kBT : kThreads;
     scale_rows<T>(sm + Ly::OFF_K, K, sFk, t0, nt);
@@ -250,6 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
+  if (a_only) {
+    if (warp == 0) tmem_dealloc(tbase, Ly::TMEM_COLS);
+    return;
+  }
 
   if (tid == 0) {
     tc_fence_after();
@@ -340,7 +346,8 @@ int launch(const void* k, const void* v, const float* beta, const float* A, cons
   {
     uint64_t dims[3] = {(uint64_t)V, (uint64_t)H, rows};
     uint64_t str[2] = {(uint64_t)V * es, (uint64_t)H * V * es};
-    int r = encode_tiled(&tv, dt, 3, v, dims, str, box, mn_sw);
+    int r = v != nullptr ? encode_tiled(&tv, dt, 3, v, dims, str, box, mn_sw) : THM_OK;
+    if (v == nullptr) tv = tk;  // build_A: no v tile is loaded
     if (r != THM_OK) return r;
   }
   if (a_mode == 0) {
@@ -873,4 +880,24 @@ extern "C" int thm_recompute_w_u_fwd(const void* k, const void* v, const float* 
   if (dtype == THM_BF16)
     return wu::dispatch<__nv_bfloat16>(k, v, beta, A, g, w, u, A_out, B, T, H, K, V, a_mode, st);
   return wu::dispatch<float>(k, v, beta, A, g, w, u, A_out, B, T, H, K, V, a_mode, st);
+}
+
+extern "C" int thm_build_A_fwd(const void* k, const float* beta, const float* g, float* A, int B, int T, int H,
+                               int K, int dtype, int sign, thm_stream_t stream) {
+  using namespace thm;
+  if (B < 0 || T < 0 || H < 0 || K <= 0 || T % 64 != 0) return THM_ERR_INVALID;
+  if (dtype != THM_F32 && dtype != THM_BF16) return THM_ERR_INVALID;
+  if (sign != -1 && sign != 1) return THM_ERR_INVALID;
+  if ((long long)B * T * H == 0) return THM_OK;
+  if (!k || !beta || !g || !A) return THM_ERR_INVALID;
+  if (!(K == 64 || K == 128)) return THM_ERR_UNSUPPORTED;
+  if (!aligned16(k)) return THM_ERR_ALIGNMENT;
+  if ((long long)B * H > 65535) return THM_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // The one-CTA-per-chunk kernel with no v tile and no w, u outputs.
+  if (dtype == THM_BF16)
+    return K == 64 ? wu::launch<__nv_bfloat16, 64, 64>(k, nullptr, beta, nullptr, g, nullptr, nullptr, A, B, T, H, sign, st)
+                   : wu::launch<__nv_bfloat16, 128, 64>(k, nullptr, beta, nullptr, g, nullptr, nullptr, A, B, T, H, sign, st);
+  return K == 64 ? wu::launch<float, 64, 64>(k, nullptr, beta, nullptr, g, nullptr, nullptr, A, B, T, H, sign, st)
+                 : wu::launch<float, 128, 64>(k, nullptr, beta, nullptr, g, nullptr, nullptr, A, B, T, H, sign, st);
 }

@@ -176,3 +176,41 @@ def gated_delta_fwd_ho(q, k, w, u, g, scale: float, h0=None, want_final: bool = 
                                             L.ptr(final), float(scale), B, T, H, K, V, L.dtype_code(q), st),
             "thm_gated_delta_fwd_ho")
     return o, final
+
+
+def build_A(k, beta, g, sign: int = -1, out=None):
+    """Per-chunk WY matrix A = (I + sign*M)^-1, M = strict_tril(beta_i k_i.k_j e^{g_i-g_j})
+    (kernels/recompute_w_u/reference.py:48-91 ``_build_A`` is sign = -1). Returns
+    A [B,T,H,64] fp32 -- the ``A`` input of ``recompute_w_u`` with a_mode 0."""
+    _cuda(k, beta, g)
+    _contig(k, beta, g)
+    B, T, H, K = k.shape
+    assert T % BT == 0, f"T={T} must be divisible by BT={BT}"
+    assert beta.shape == (B, T, H) and g.shape == (B, T, H)
+    assert beta.dtype == torch.float32 and g.dtype == torch.float32
+    assert sign in (-1, 1)
+    if out is None:
+        out = torch.empty(B, T, H, BT, device=k.device, dtype=torch.float32)
+    assert out.shape == (B, T, H, BT) and out.dtype == torch.float32 and out.is_contiguous()
+    st = L.stream_of(k)
+    L.check(L.load().thm_build_A_fwd(L.ptr(k), L.ptr(beta), L.ptr(g), L.ptr(out), B, T, H, K, L.dtype_code(k),
+                                     int(sign), st), "thm_build_A_fwd")
+    return out
+
+
+def chunk_local_cumsum(g_inc, scale: float = 1.0, out=None):
+    """g[b, c*64+i, h] = scale * sum_{j<=i} g_inc[b, c*64+j, h] per 64-token chunk: the
+    chunk-local cumulative gate the reference's generators build
+    (kernels/chunk_fwd_h/reference.py:41-45). ``out`` may be ``g_inc`` (in place)."""
+    _cuda(g_inc)
+    _contig(g_inc)
+    assert g_inc.dtype == torch.float32 and g_inc.dim() == 3, "g_inc must be [B,T,H] float32"
+    B, T, H = g_inc.shape
+    assert T % BT == 0, f"T={T} must be divisible by BT={BT}"
+    if out is None:
+        out = torch.empty_like(g_inc)
+    assert out.shape == g_inc.shape and out.dtype == torch.float32 and out.is_contiguous()
+    st = L.stream_of(g_inc)
+    L.check(L.load().thm_chunk_local_cumsum_fwd(L.ptr(g_inc), L.ptr(out), B, T, H, float(scale), st),
+            "thm_chunk_local_cumsum_fwd")
+    return out
