@@ -117,6 +117,8 @@ int thm_chunk_local_cumsum_fwd(const float* g_inc, float* g, int B, int T, int H
  *     h_{c+1} = exp(g_last) h_c + (k_c * exp(g_last - g_c))^T v_new_c
  *   h[b,c,h] = h_c (state BEFORE chunk c); `v` is u; v_new (optional)
  *   [B,T,H,V] in `dtype`; final_state (optional) [B,H,K,V] fp32 = h_NT.
+ *   In mode 1 h may be NULL (no per-chunk states are written), e.g. when
+ *   only the final state of a sequence segment is wanted.
  * k, w [B,T,H,K], v [B,T,H,V] in `dtype`; g [B,T,H] fp32;
  * h [B,T/64,H,K,V] in `h_dtype` (THM_F32 as the reference, or THM_BF16: the
  * state itself is always carried in fp32, only the stored copy is rounded);

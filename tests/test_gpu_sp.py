@@ -1,0 +1,82 @@
+"""GPU parity of the sequence-parallel delta rule (theorem_b200.sp) on one GPU:
+segment summaries against the oracle, and the segmented layer forward against the
+unsegmented kernel and the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops as orc
+from tests.harness import assert_close
+from tests.synth import deltanet_inputs
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL = 2e-2
+
+
+def _inputs(B, T, H, K, V, seed, dtype=torch.bfloat16):
+    d = deltanet_inputs(B, T, H, K, V, seed, dtype=dtype)
+    q, k, v, beta, g = d["q"], d["k"], d["v"], d["beta"], d["g"]
+    A = orc.build_A(k.float(), beta, g, 1)
+    w, u = orc.recompute_w_u(k.float(), v.float(), beta, A, g)
+    gen = torch.Generator().manual_seed(seed + 7)
+    h0 = torch.randn(B, H, K, V, generator=gen) * 0.3
+    return q, k, torch.from_numpy(w).to(dtype), torch.from_numpy(u).to(dtype), g, h0
+
+
+def test_segment_summary_matches_oracle():
+    from theorem_b200 import sp
+    q, k, w, u, g, _ = _inputs(2, 512, 2, 128, 128, seed=1)
+    M, S = sp.segment_summary(k.to(DEV), w.to(DEV), u.to(DEV), g.to(DEV))
+    eye = np.broadcast_to(np.eye(128), (2, 2, 128, 128)).copy()
+    _, _, rM = orc.chunk_fwd_h_delta(k.float(), w.float(), np.zeros((2, 512, 2, 128)), g, eye)
+    _, _, rS = orc.chunk_fwd_h_delta(k.float(), w.float(), u.float(), g, None)
+    assert_close(M.cpu().double(), torch.from_numpy(rM), TOL, TOL, "M")
+    assert_close(S.cpu().double(), torch.from_numpy(rS), TOL, TOL, "S")
+
+
+@pytest.mark.parametrize("R", [1, 2, 4, 8])
+def test_segmented_forward_matches_unsegmented(R):
+    from theorem_b200 import ops, sp
+    q, k, w, u, g, h0 = (t.to(DEV) for t in _inputs(1, 4096, 4, 128, 128, seed=2))
+    scale = 128 ** -0.5
+    o_ref, f_ref = ops.gated_delta_fwd_ho(q, k, w, u, g, scale, h0=h0, want_final=True)
+    o, f = sp.sp_forward_local(q, k, w, u, g, scale, R, h0=h0)
+    assert o.shape == o_ref.shape and f.shape == f_ref.shape
+    assert_close(o.float().cpu(), o_ref.float().cpu(), TOL, TOL, f"o R={R}")
+    assert_close(f.cpu(), f_ref.cpu(), TOL, TOL, f"final R={R}")
+
+
+def test_segmented_forward_matches_oracle():
+    from theorem_b200 import sp
+    q, k, w, u, g, h0 = _inputs(2, 1024, 2, 128, 128, seed=3)
+    scale = 128 ** -0.5
+    o, f = sp.sp_forward_local(*(t.to(DEV) for t in (q, k, w, u, g)), scale, 4, h0=h0.to(DEV))
+    bf = lambda a: torch.from_numpy(np.asarray(a)).to(torch.bfloat16).double().numpy()  # noqa: E731
+    h, vn, fin = orc.chunk_fwd_h_delta(k.float(), w.float(), u.float(), g, h0)
+    ro = orc.chunk_fwd_o(q.float(), k.float(), bf(vn), g, h, scale)
+    assert_close(o.float().cpu().double(), torch.from_numpy(ro), TOL, TOL, "o")
+    assert_close(f.cpu().double(), torch.from_numpy(fin), TOL, TOL, "final")
+
+
+def test_segmented_forward_fp32_separate_kernels():
+    """fp32, K = V = 64: pass 3 runs chunk_fwd_h -> chunk_fwd_o (no fused kernel)."""
+    from theorem_b200 import sp
+    q, k, w, u, g, h0 = _inputs(1, 512, 2, 64, 64, seed=4, dtype=torch.float32)
+    scale = 64 ** -0.5
+    o, f = sp.sp_forward_local(*(t.to(DEV) for t in (q, k, w, u, g)), scale, 4, h0=h0.to(DEV))
+    h, vn, fin = orc.chunk_fwd_h_delta(k, w, u, g, h0)
+    ro = orc.chunk_fwd_o(q, k, vn, g, h, scale)
+    assert_close(o.cpu().double(), torch.from_numpy(ro), TOL, TOL, "o")
+    assert_close(f.cpu().double(), torch.from_numpy(fin), TOL, TOL, "final")
+
+
+def test_delta_h_without_state_output():
+    """chunk_fwd_h mode 1 with h = NULL writes only v_new / final."""
+    from theorem_b200 import ops
+    q, k, w, u, g, h0 = (t.to(DEV) for t in _inputs(2, 256, 2, 128, 128, seed=5))
+    h, vn, fin = ops.chunk_fwd_h(k, u, g, w=w, h0=h0, mode=1, want_v_new=True, want_final=True)
+    none, vn2, fin2 = ops.chunk_fwd_h(k, u, g, w=w, h0=h0, mode=1, want_v_new=True, want_final=True,
+                                      want_h=False)
+    assert none is None
+    assert torch.equal(vn, vn2) and torch.equal(fin, fin2)

@@ -35,6 +35,8 @@ namespace chunk_h {
 constexpr int kThreads = 128;
 constexpr int kBT = 64;
 constexpr int kVT = 64;
+constexpr int kStoreVn = 1;  // flags: v_new is written
+constexpr int kStoreH = 2;   // flags: h is written (always in mode 0)
 
 template <typename T, int K, int MODE, bool HB>
 struct Layout {
@@ -90,7 +92,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     chunk_fwd_h_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_hst,
                        const __grid_constant__ CUtensorMap tm_vn, const float* __restrict__ g,
-                       const float* __restrict__ h0, float* __restrict__ final_state, int has_vn, int T_len,
+                       const float* __restrict__ h0, float* __restrict__ final_state, int flags, int T_len,
                        int H, int V) {
   using Ly = Layout<T, K, MODE, HB>;
   using HT = typename std::conditional<HB, __nv_bfloat16, float>::type;
@@ -218,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if constexpr (MODE == 1) {
       if (tid == 0) {
-        store_h(c);
+        if (flags & kStoreH) store_h(c);
         tc_fence_after();
 #pragma unroll
         for (int q = 0; q < K / kStep; ++q) {
@@ -295,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // U_c = k^T (scaled v / v_new) -- A = k^T (MN-major), B = v (MN-major)
     if (tid == 0) {
-      if (MODE == 1 && has_vn) {
+      if (MODE == 1 && (flags & kStoreVn)) {
 #pragma unroll
         for (int j = 0; j < kVT / kBox; ++j)
           tma_store_3d(&tm_vn, sm + Ly::OFF_VN + j * kBT * 128, v0 + j * kBox, hh, row0);
@@ -408,16 +410,18 @@ int launch(const void* k, const void* w, const void* v, const float* g, const fl
     uint64_t str[1] = {(uint64_t)V * hes};
     uint32_t hbox[2] = {(uint32_t)(128 / hes), (uint32_t)K};
     const CUtensorMapSwizzle hsw = (Ly::H_FROM_S && !bf) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
-    int r = encode_tiled(&th, HB ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, h, dims,
-                         str, hbox, hsw);
+    int r = h != nullptr ? encode_tiled(&th, HB ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                        2, h, dims, str, hbox, hsw)
+                         : THM_OK;
+    if (h == nullptr) th = tk;  // delta mode without the h output: no h store is issued
     if (r != THM_OK) return r;
   }
   auto kern = chunk_fwd_h_kernel<T, K, MODE, HB>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
     return THM_ERR_CUDA;
   dim3 grid(V / kVT, B * H);
-  kern<<<grid, kThreads, Ly::SMEM, st>>>(tk, tv, tw, th, tvn, g, h0, final_state, v_new != nullptr ? 1 : 0, T_len,
-                                         H, V);
+  const int flags = (v_new != nullptr ? kStoreVn : 0) | (h != nullptr ? kStoreH : 0);
+  kern<<<grid, kThreads, Ly::SMEM, st>>>(tk, tv, tw, th, tvn, g, h0, final_state, flags, T_len, H, V);
   return check_launch();
 }
 
@@ -457,9 +461,9 @@ extern "C" int thm_chunk_fwd_h_fwd(const void* k, const void* w, const void* v, 
     }
     return THM_OK;
   }
-  if (!k || !v || !g || !h) return THM_ERR_INVALID;
+  if (!k || !v || !g || (!h && mode == 0)) return THM_ERR_INVALID;
   if (!(K == 64 || K == 128) || !(V == 64 || V == 128)) return THM_ERR_UNSUPPORTED;
-  if (!aligned16(k) || !aligned16(v) || !aligned16(h) || (w && !aligned16(w)) || (h0 && !aligned16(h0)) ||
+  if (!aligned16(k) || !aligned16(v) || (h && !aligned16(h)) || (w && !aligned16(w)) || (h0 && !aligned16(h0)) ||
       (v_new && !aligned16(v_new)) || (final_state && !aligned16(final_state)))
     return THM_ERR_ALIGNMENT;
   if ((long long)B * H > 65535) return THM_ERR_UNSUPPORTED;

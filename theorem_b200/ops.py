@@ -86,14 +86,15 @@ def recompute_w_u(k, v, beta, A, g, a_mode: int = 0, w=None, u=None, A_out=None)
 
 
 def chunk_fwd_h(k, v, g, w=None, h0=None, mode: int = 0, want_v_new: bool = False,
-                want_final: bool = False, h=None, v_new=None, h_dtype=torch.float32):
+                want_final: bool = False, h=None, v_new=None, h_dtype=torch.float32, want_h: bool = True):
     """Inter-chunk state recurrence (kernels/chunk_fwd_h/kernel.py:141-191).
 
     mode 0: reference recurrence, returns h [B,NT,H,K,V] of post-update states.
     mode 1: gated delta rule (``v`` is u, ``w`` required), returns
     (h of states entering each chunk, v_new or None, final or None).
     h is stored in ``h_dtype`` (float32, or bfloat16 for the chain); the state
-    itself is carried in fp32.
+    itself is carried in fp32. ``want_h=False`` (mode 1) writes no per-chunk
+    states and returns None for h.
     """
     _cuda(k, v, g, w, h0)
     _contig(k, v, g, w, h0)
@@ -103,9 +104,11 @@ def chunk_fwd_h(k, v, g, w=None, h0=None, mode: int = 0, want_v_new: bool = Fals
     assert v.shape == (B, T, H, V) and v.dtype == k.dtype and g.shape == (B, T, H)
     assert g.dtype == torch.float32
     NT = T // BT
-    if h is None:
+    assert want_h or mode == 1, "the reference recurrence (mode 0) always returns h"
+    if h is None and want_h:
         h = torch.empty(B, NT, H, K, V, device=k.device, dtype=h_dtype)
-    assert h.shape == (B, NT, H, K, V) and h.dtype in (torch.float32, torch.bfloat16) and h.is_contiguous()
+    if h is not None:
+        assert h.shape == (B, NT, H, K, V) and h.dtype in (torch.float32, torch.bfloat16) and h.is_contiguous()
     final = None
     if mode == 1:
         assert w is not None and w.shape == k.shape and w.dtype == k.dtype
@@ -122,7 +125,7 @@ def chunk_fwd_h(k, v, g, w=None, h0=None, mode: int = 0, want_v_new: bool = Fals
     st = L.stream_of(k)
     L.check(L.load().thm_chunk_fwd_h_fwd(L.ptr(k), L.ptr(w), L.ptr(v), L.ptr(g), L.ptr(h0), L.ptr(h),
                                          L.ptr(v_new), L.ptr(final), B, T, H, K, V, L.dtype_code(k),
-                                         L.dtype_code(h), int(mode), st),
+                                         L.dtype_code(h) if h is not None else L.dtype_code(k), int(mode), st),
             "thm_chunk_fwd_h_fwd")
     if mode == 1:
         return h, v_new, final
