@@ -451,6 +451,82 @@ def profile_op(args) -> int:
     return 0
 
 
+# ---------------------------------------------------------------------------
+# sequence-parallel variant (BASELINE config 5 SP: B=1, T=131072), --sp
+# ---------------------------------------------------------------------------
+SP_CFG = dict(B=1, T=131072, H=16, K=128, V=128)
+
+
+def run_sp(args, rank, world, device):
+    """State recurrence + output of one long sequence split along T: each rank
+    holds T/N tokens cut into --sp-segments local segments (strong scaling);
+    the only exchange is the all_gather of per-rank (M, S) summaries."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+    from theorem_b200 import ops, sp
+    from theorem_b200 import dist as D
+    c = SP_CFG
+    B, T, H, K, V = c["B"], c["T"], c["H"], c["K"], c["V"]
+    R = args.sp_segments
+    gen = torch.Generator(device=device).manual_seed(4321)
+    q = F.normalize(torch.randn(B, T, H, K, generator=gen, device=device), dim=-1).bfloat16()
+    k = F.normalize(torch.randn(B, T, H, K, generator=gen, device=device), dim=-1).bfloat16()
+    v = torch.randn(B, T, H, V, generator=gen, device=device).bfloat16()
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=gen, device=device))
+    inc = F.logsigmoid(torch.randn(B, T, H, generator=gen, device=device)) / 16
+    gate = ops.chunk_local_cumsum(inc)
+    w, u = ops.recompute_w_u(k, v, beta, None, gate, a_mode=1)
+    del v
+    scale = K ** -0.5
+    Tr = T // world
+    part = lambda t: t[:, rank * Tr:(rank + 1) * Tr].contiguous()  # noqa: E731
+    qr, kr, wr, ur, gr = (part(t) for t in (q, k, w, u, gate))
+
+    def step():
+        if world == 1:
+            return sp.sp_forward_local(qr, kr, wr, ur, gr, scale, R)
+        return sp.sp_forward(qr, kr, wr, ur, gr, scale, local_segments=R)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        o_r, fin = step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = D.max_over_ranks(e0.elapsed_time(e1) / args.steps, device=device)
+    # Check: the gathered o of all ranks against the one-GPU segmented run on rank 0.
+    parts = [torch.empty_like(o_r) for _ in range(world)] if world > 1 else [o_r]
+    if world > 1:
+        dist.all_gather(parts, o_r)
+    out = {}
+    if rank == 0:
+        o_all = torch.cat(parts, dim=1)
+        o_chk, _ = sp.sp_forward_local(q, k, w, u, gate, scale, R * world)
+        out["check_max_abs_diff_vs_1gpu_segmented"] = float((o_all.float() - o_chk.float()).abs().max())
+        if world == 1:
+            # the same sequence through the unsegmented fused kernel (B*H = 16 CTAs)
+            for _ in range(2):
+                ops.gated_delta_fwd_ho(q, k, w, u, gate, scale)
+            torch.cuda.synchronize()
+            a, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            o_un, _ = ops.gated_delta_fwd_ho(q, k, w, u, gate, scale)
+            b2.record()
+            torch.cuda.synchronize()
+            out["unsegmented_fused_ms"] = a.elapsed_time(b2)
+            out["check_max_abs_diff_vs_unsegmented"] = float((o_r.float() - o_un.float()).abs().max())
+    status = __import__("theorem_b200._lib", fromlist=["x"]).device_status()
+    assert status == 0, f"in-kernel wait timed out (status {status})"
+    return ms, out
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -466,6 +542,9 @@ def main(argv=None) -> int:
                                      "chunk_fwd_o_hf32", "causal_conv1d_bds"],
                     help="profiling mode: launch one op (bf16, chain settings) --iters times and exit")
     ap.add_argument("--shape", default="2,4096,16,128,128", help="B,T,H,K,V for --op")
+    ap.add_argument("--sp", action="store_true",
+                    help="sequence-parallel variant: one B=1, T=131072 sequence split along T over the ranks")
+    ap.add_argument("--sp-segments", type=int, default=8, help="local segments per rank for --sp")
     ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args(argv)
     if args.op:
@@ -488,6 +567,25 @@ def main(argv=None) -> int:
         D.init("nccl", timeout_s=120.0, device=device)
     from theorem_b200 import _lib
     _lib.load()
+
+    if args.sp:
+        ms, out = run_sp(args, rank, world, device)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            c = SP_CFG
+            line = {"metric": "sp_gated_delta_tokens_per_s", "value": c["T"] * c["B"] / (ms / 1e3), "unit": "tokens/s",
+                    "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                    "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                    "data": "synthetic",
+                    "config": {"workload": "BASELINE config 5 SP variant: state recurrence + output of one sequence "
+                                           "(inputs q, k, w, u, g resident)", **c,
+                               "parallelism": f"sp{world} x {args.sp_segments} local segments",
+                               "collective": "all_gather of per-rank (M, S) summaries"},
+                    "gpu_launches": 3 * args.steps, **out}
+            print(json.dumps(line), flush=True)
+        return 0
 
     res = run_chain(args, rank, world, device)
     pk = peaks()

@@ -15,8 +15,13 @@ TOL = 2e-2
 
 
 def _inputs(B, T, H, K, V, seed, dtype=torch.bfloat16):
+    """Chain-like inputs with a slow gate (about -0.1 per chunk), so that a state
+    carried across a segment boundary still matters many chunks later."""
     d = deltanet_inputs(B, T, H, K, V, seed, dtype=dtype)
-    q, k, v, beta, g = d["q"], d["k"], d["v"], d["beta"], d["g"]
+    q, k, v, beta = d["q"], d["k"], d["v"], d["beta"]
+    gen = torch.Generator().manual_seed(seed + 11)
+    inc = -0.003 * torch.rand(B, T, H, generator=gen) - 0.0002
+    g = inc.reshape(B, T // 64, 64, H).cumsum(2).reshape(B, T, H).contiguous()
     A = orc.build_A(k.float(), beta, g, 1)
     w, u = orc.recompute_w_u(k.float(), v.float(), beta, A, g)
     gen = torch.Generator().manual_seed(seed + 7)

@@ -26,10 +26,13 @@ def _inputs():
     from tests.synth import deltanet_inputs
     from oracle import ops as orc
     d = deltanet_inputs(2, 512, 2, 64, 48, seed=12, dtype=torch.float32)
-    A = orc.build_A(d["k"], d["beta"], d["g"], 1)
-    w, u = orc.recompute_w_u(d["k"], d["v"], d["beta"], A, d["g"])
+    # slow gate (about -0.1 per chunk): the state entering a segment still matters
+    inc = -0.003 * torch.rand(2, 512, 2, generator=torch.Generator().manual_seed(5)) - 0.0002
+    g = inc.reshape(2, 8, 64, 2).cumsum(2).reshape(2, 512, 2)
+    A = orc.build_A(d["k"], d["beta"], g, 1)
+    w, u = orc.recompute_w_u(d["k"], d["v"], d["beta"], A, g)
     h0 = np.random.default_rng(3).standard_normal((2, 2, 64, 48)) * 0.3
-    return d["k"].double().numpy(), w, u, d["g"].double().numpy(), h0
+    return d["k"].double().numpy(), w, u, g.double().numpy(), h0
 
 
 def _worker_sp(rank, ws, port, q):
@@ -46,6 +49,8 @@ def _worker_sp(rank, ws, port, q):
     h_pre, _, fin = orc.chunk_fwd_h_delta(k, w, u, g, h0)
     expect = h_pre[:, rank * L // 64]
     ok = bool(np.allclose(h_start.numpy(), expect, rtol=1e-9, atol=1e-9))
+    if rank > 0:  # the carried state is visible: starting from 0 instead would be wrong
+        ok = ok and not np.allclose(sp.prefix_state(Ms, Ss, rank, None).numpy() * 0, expect, atol=1e-3)
     fin_ok = True
     if rank == ws - 1:
         h_end = torch.matmul(M, h_start) + S

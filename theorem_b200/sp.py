@@ -57,12 +57,16 @@ def prefix_states(Ms, Ss, h0=None):
     the first (None = 0)."""
     R, B, H, K, V = Ss.shape
     dt = _acc_dtype(Ss)
-    h = torch.zeros(B, H, K, V, dtype=dt, device=Ss.device) if h0 is None else h0.to(dt).clone()
-    out = []
-    for r in range(R):
-        out.append(h)
-        h = torch.matmul(Ms[r].to(dt), h) + Ss[r].to(dt)
-    return torch.stack(out)
+    out = torch.empty(R, B * H, K, V, dtype=dt, device=Ss.device)
+    if h0 is None:
+        out[0].zero_()
+    else:
+        out[0].copy_(h0.reshape(B * H, K, V))
+    Mf = Ms.to(dt).reshape(R, B * H, K, K)
+    Sf = Ss.to(dt).reshape(R, B * H, K, V)
+    for r in range(1, R):
+        torch.baddbmm(Sf[r - 1], Mf[r - 1], out[r - 1], out=out[r])  # h_r = M h_{r-1} + S
+    return out.reshape(R, B, H, K, V)
 
 
 def prefix_state(Ms, Ss, upto: int, h0=None):
