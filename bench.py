@@ -443,6 +443,7 @@ def profile_op(args) -> int:
         "recompute_w_u": lambda: ops.recompute_w_u(k, v, beta, None, gate, a_mode=1, w=w, u=u),
         "chunk_fwd_h": lambda: ops.chunk_fwd_h(k, u, gate, w=w, mode=1, h=h, v_new=vn),
         "chunk_fwd_o": lambda: ops.chunk_fwd_o(q, k, vn, gate, h, K ** -0.5),
+        "gated_delta_ho": lambda: ops.gated_delta_fwd_ho(q, k, w, u, gate, K ** -0.5),
     }
     for _ in range(args.iters):
         fns[args.op]()
@@ -539,7 +540,7 @@ def main(argv=None) -> int:
     ap.add_argument("--unfused", action="store_true",
                     help="run chunk_fwd_h -> chunk_fwd_o as two kernels instead of the fused gated_delta_ho")
     ap.add_argument("--op", choices=["causal_conv1d", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o",
-                                     "chunk_fwd_o_hf32", "causal_conv1d_bds"],
+                                     "chunk_fwd_o_hf32", "causal_conv1d_bds", "gated_delta_ho"],
                     help="profiling mode: launch one op (bf16, chain settings) --iters times and exit")
     ap.add_argument("--shape", default="2,4096,16,128,128", help="B,T,H,K,V for --op")
     ap.add_argument("--sp", action="store_true",
