@@ -116,3 +116,28 @@ def test_unsupported_shapes_raise():
     g = torch.zeros(1, 64, 1, device=DEV)
     with pytest.raises(AssertionError):
         ops.gated_delta_fwd_ho(z(1, 64, 1, 64), z(1, 64, 1, 64), z(1, 64, 1, 64), z(1, 64, 1, 64), g, 0.1)
+
+
+def test_forward_from_host_pipelined_equals_device_path():
+    """Pinned host in / host out, 4 groups of sequences pipelined over copy streams:
+    the same o (bit for bit) and final states as the device-resident call."""
+    from theorem_b200.chain import GatedDeltaNetForward
+    B, T, H, K = 8, 256, 2, 128
+    D = H * K
+    gen = torch.Generator().manual_seed(6)
+    xs = [torch.randn(B, T, D, generator=gen).to(torch.bfloat16) for _ in range(3)]
+    cw = [(torch.randn(D, 4, generator=gen) * 0.5).to(DEV) for _ in range(3)]
+    cb = [(torch.randn(D, generator=gen) * 0.3).to(DEV) for _ in range(3)]
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=gen))
+    inc = torch.nn.functional.logsigmoid(torch.randn(B, T, H, generator=gen)) / 16
+    g = inc.reshape(B, T // 64, 64, H).cumsum(2).reshape(B, T, H).contiguous()
+    h0 = torch.randn(B, H, K, K, generator=gen) * 0.1
+    layer = GatedDeltaNetForward(H, K, K, cw, cb)
+    o_dev, f_dev = layer(*(x.to(DEV) for x in xs), beta.to(DEV), g.to(DEV), h0=h0.to(DEV))
+    host = [t.pin_memory() for t in (*xs, beta, g)]
+    o_host = torch.empty(B, T, H, K, dtype=torch.bfloat16).pin_memory()
+    out, fin = layer.forward_from_host(*host, o_host, slices=4, h0=h0.to(DEV))
+    torch.cuda.synchronize()
+    assert out.data_ptr() == o_host.data_ptr()
+    assert torch.equal(o_host, o_dev.cpu())
+    assert torch.equal(fin.cpu(), f_dev.cpu())

@@ -82,3 +82,57 @@ class GatedDeltaNetForward:
                                         h=bf["h"], v_new=v)
         o = ops.chunk_fwd_o(q, k, v_new, g, h, self.scale, o=out)
         return o, fin
+
+    def forward_from_host(self, xq, xk, xv, beta, g, out, slices: int = 4, h0=None):
+        """The layer forward for inputs and output in pinned host memory.
+
+        The batch is cut into ``slices`` groups of sequences and pipelined over three
+        streams: the host-to-device copy of group i+1 and the device-to-host copy of
+        group i-1 run while group i computes (PCIe is full duplex). Device staging is
+        double-buffered; all compute stays on the caller's current stream, which on
+        return is ordered after the last copy. Returns ``out`` (and the final states
+        [B,H,K,V] fp32 when ``h0`` is given)."""
+        B, T, D = xq.shape
+        assert B % slices == 0, "B must split into equal groups"
+        assert all(t.is_pinned() for t in (xq, xk, xv, beta, g, out)), "host tensors must be pinned"
+        bs = B // slices
+        dev = torch.device("cuda", torch.cuda.current_device())
+        comp = torch.cuda.current_stream(dev)
+        if getattr(self, "_host_streams", None) is None:
+            self._host_streams = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+        s_in, s_out = self._host_streams
+        hosts = (xq, xk, xv, beta, g)
+        stage = [[torch.empty((bs,) + tuple(t.shape[1:]), dtype=t.dtype, device=dev) for t in hosts] for _ in range(2)]
+        ostage = [torch.empty((bs,) + tuple(out.shape[1:]), dtype=out.dtype, device=dev) for _ in range(2)]
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_comp = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
+        finals = []
+        for i in range(slices):
+            j = i & 1
+            lo, hi = i * bs, (i + 1) * bs
+            if i >= 2:
+                s_in.wait_event(ev_comp[j])  # group i-2 no longer reads this staging set
+            with torch.cuda.stream(s_in):
+                for d_, h_ in zip(stage[j], hosts):
+                    d_.copy_(h_[lo:hi], non_blocking=True)
+            ev_in[j].record(s_in)
+            comp.wait_event(ev_in[j])
+            if i >= 2:
+                comp.wait_event(ev_out[j])  # group i-2's output has left this buffer
+            _, fin = self(*stage[j], h0=None if h0 is None else h0[lo:hi], out=ostage[j],
+                          final_state=h0 is not None)
+            if fin is not None:
+                finals.append(fin)
+            ev_comp[j].record(comp)
+            s_out.wait_event(ev_comp[j])
+            with torch.cuda.stream(s_out):
+                out[lo:hi].copy_(ostage[j], non_blocking=True)
+            ev_out[j].record(s_out)
+        comp.wait_stream(s_out)
+        comp.wait_stream(s_in)
+        for t in stage[0] + stage[1] + ostage:
+            t.record_stream(comp)
+        if h0 is not None:
+            return out, torch.cat(finals, 0)
+        return out
