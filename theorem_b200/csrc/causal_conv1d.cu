@@ -388,25 +388,61 @@ struct Layout {
   static constexpr int SMEM = OFF_BAR + 64 + 1024;
 };
 
+// One row of the thread's 4 channels: shared memory <-> fp32 registers.
+template <typename T>
+__device__ __forceinline__ void load_row(const uint8_t* p, float* f) {
+  if constexpr (sizeof(T) == 2) {
+    const uint2 r = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
+    const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
+    f[0] = a.x; f[1] = a.y; f[2] = c.x; f[3] = c.y;
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_row(uint8_t* p, const float* f) {
+  if constexpr (sizeof(T) == 2) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]));
+  } else {
+    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+  }
+}
+
+// silu for bf16 outputs: x sigmoid(x) = h + h tanh(h), h = x/2, with the
+// hardware tanh approximation (relative error ~2^-11, below bf16's 2^-9
+// output rounding). fp32 outputs keep silu_f.
+__device__ __forceinline__ float silu_tanh(float x) {
+  const float h = 0.5f * x;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+  return fmaf(h, t, h);
+}
+
 template <typename T, int W, bool SILU, int GL>
 __global__ void __launch_bounds__(kThreads, 2)
     conv_bsd_tma(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_o,
                  const float* __restrict__ w, const float* __restrict__ bias, int S, int D) {
   using Ly = Layout<T, W>;
+  constexpr int C = 4;                           // channels per thread
+  constexpr int NCG = kCh / C;                   // channel groups across the 256 channels
+  constexpr int RPT = kRows / (kThreads / NCG);  // rows per thread per tile (8)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + Ly::OFF_BAR);
   const int tid = threadIdx.x;
-  const int cg = tid & 63, rq = tid >> 6;  // channel group (4 ch), row quarter (8 rows)
+  const int cg = tid % NCG, rq = tid / NCG;  // channel group, row band
   const int c0 = blockIdx.x * kCh;
   const int t_begin = blockIdx.y * kStrip;
   const int b = blockIdx.z;
   const int ntiles = min(kStrip, S - t_begin + kRows - 1) / kRows;
-  const int cc = min(c0 + 4 * cg, D - 4);  // clamp: channels past D are computed but not stored
+  const int cc = min(c0 + C * cg, D - C);  // clamp: channels past D are computed but not stored
 
-  float wr[4][W], bs[4];
+  float wr[C][W], bs[C];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < C; ++j) {
     bs[j] = __ldg(bias + cc + j);
 #pragma unroll
     for (int k = 0; k < W; ++k) wr[j][k] = __ldg(w + (long long)(cc + j) * W + k);
@@ -434,35 +470,31 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (!ok) break;
     const uint8_t* in = sm + st * Ly::IN_STRIDE;
     uint8_t* out = sm + Ly::OFF_OUT + ob * Ly::OUT_BYTES;
-    // rows r0-W+1 .. r0+7 of this tile (smem row = tile row + W - 1)
-    float xr[8 + W - 1][4];
+    // rows r0-W+1 .. r0+RPT-1 of this band (smem row = tile row + W - 1)
+    float xr[RPT + W - 1][C];
 #pragma unroll
-    for (int j = 0; j < 8 + W - 1; ++j) {
-      Vec4<T> v;
-      v.raw_from_smem(in + ((8 * rq + j) * kCh + 4 * cg) * Ly::ES);
-      v.to_float(xr[j]);
-    }
+    for (int j = 0; j < RPT + W - 1; ++j) load_row<T>(in + ((RPT * rq + j) * kCh + C * cg) * Ly::ES, xr[j]);
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      float o[4];
+    for (int r = 0; r < RPT; ++r) {
+      float o[C];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < C; ++j) {
         float acc = bs[j];
 #pragma unroll
         for (int k = 0; k < W; ++k) acc = fmaf(xr[r + k][j], wr[j][k], acc);
-        o[j] = SILU ? silu_f(acc) : acc;
+        o[j] = SILU ? (sizeof(T) == 2 ? silu_tanh(acc) : silu_f(acc)) : acc;
       }
       if (GL > 0) {
         float ss = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) ss = fmaf(o[j], o[j], ss);
+        for (int j = 0; j < C; ++j) ss = fmaf(o[j], o[j], ss);
 #pragma unroll
         for (int m = 1; m < GL; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
         const float rn = rsqrtf(ss + 1e-6f);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) o[j] *= rn;
+        for (int j = 0; j < C; ++j) o[j] *= rn;
       }
-      Vec4<T>::store_smem(out + ((8 * rq + r) * kCh + 4 * cg) * Ly::ES, o);
+      store_row<T>(out + ((RPT * rq + r) * kCh + C * cg) * Ly::ES, o);
     }
     fence_proxy_async_smem();
     __syncthreads();
