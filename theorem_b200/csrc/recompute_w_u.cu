@@ -643,8 +643,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&tfree_k[grp]);
         const int r0 = 16 * sp + (lane >> 2), r1 = r0 + 8;
         const float b0 = sc[r0], b1 = sc[r1], g0 = sc[64 + r0], g1 = sc[64 + r1];
+        // Only the strictly lower triangle of M is ever read (the solve below and
+        // T = M10 A00): this warp's rows 16sp..16sp+15 need column groups j <= 2sp+1.
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
+          if (j > 2 * sp + 1) break;  // warp-uniform
           const int cc = 8 * j + 2 * (lane & 3);
           const float gc0 = sc[64 + cc], gc1 = sc[64 + cc + 1];
           float2 m0, m1;
