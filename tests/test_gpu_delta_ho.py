@@ -141,3 +141,22 @@ def test_forward_from_host_pipelined_equals_device_path():
     assert out.data_ptr() == o_host.data_ptr()
     assert torch.equal(o_host, o_dev.cpu())
     assert torch.equal(fin.cpu(), f_dev.cpu())
+
+
+def test_steep_gates_take_the_direct_decay_path():
+    """Chunks whose gates span more than 120 (in log space) form P with one
+    exponential per entry instead of the two-factor decay; both must agree with
+    the oracle."""
+    from theorem_b200 import ops
+    B, T, H = 1, 256, 2
+    q, k, w, u, g, h0 = _inputs(B, T, H, seed=41)
+    gen = torch.Generator().manual_seed(42)
+    inc = -3.0 * torch.rand(B, T, H, generator=gen)  # ~ -96 per chunk on average, up to ~-190
+    inc[:, :64] *= 0.01                               # first chunk: gentle (factored path)
+    g = inc.reshape(B, T // 64, 64, H).cumsum(2).reshape(B, T, H).contiguous()
+    scale = 128 ** -0.5
+    o, fin = ops.gated_delta_fwd_ho(*_dev(q, k, w, u, g), scale, h0=_dev(h0)[0], want_final=True)
+    ro, rfin = _oracle(q, k, w, u, g, h0, scale)
+    assert torch.isfinite(o.float()).all()
+    assert_close(o.float().cpu().double(), torch.from_numpy(ro), TOL, TOL, "o")
+    assert_close(fin.cpu().double(), torch.from_numpy(rfin), TOL, TOL, "final state")

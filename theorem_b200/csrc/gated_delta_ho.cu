@@ -4,30 +4,36 @@
 // The reference runs the two as separate kernels that meet in HBM
 // (kernels/chunk_fwd_h/kernel.py:61-138 writes h, kernels/chunk_fwd_o/
 // kernel.py:52-136 reads it back; docs/ARCHITECTURE.md:200-235 chains
-// recompute_w_u -> chunk_fwd_h -> chunk_fwd_o). Here one CTA of 256 threads
-// owns one (b, h) sequence (K = V = 128, bf16 activations) and walks its
-// chunks in order; neither the per-chunk states h nor v_new ever reach HBM.
-// Per chunk c, with the fp32 state h_c in registers (thread <-> row d of the
-// state, one 64-column half per warpgroup) and a bf16 copy in shared memory:
+// recompute_w_u -> chunk_fwd_h -> chunk_fwd_o). Here one CTA owns one (b, h)
+// sequence (K = V = 128, bf16 activations) and walks its chunks in order;
+// neither the per-chunk states h nor v_new ever reach HBM. Per chunk c, with
+// the fp32 state h_c in registers (thread <-> state row d, one 64-column half
+// per warpgroup) and a bf16 copy of it in shared memory:
 //
-//   S     = q k^T                           tcgen05 (M=64,  N=64,  K=128)
-//   X     = w h_c,  G = q h_c               tcgen05 (M=64,  N=128, K=128)
-//   P     = tril(S * e^{g_t - g_s})         TMEM -> registers -> smem (bf16)
-//   v_new = u - X                            TMEM -> registers -> smem (bf16)
-//   U     = k^T (v_new * e^{g_last - g_t})  tcgen05 (M=128, N=128, K=64)
-//   L     = P v_new                          tcgen05 (M=64,  N=128, K=64)
-//   h_{c+1} = e^{g_last} h_c + U             registers
-//   o_c   = scale (L + e^{g_t} G)            registers -> smem -> TMA store
+//   [X; G] = [w; q] h_c                  tcgen05 M=128, N=128, K=128
+//   [.; S] = [w; q] k^T                  tcgen05 M=128, N=64,  K=128 (rows 64..127)
+//   v_new  = u - X                        rows t on TMEM lanes 0..63
+//   P      = tril(S * e^{g_t - g_s})      rows t on TMEM lanes 64..127
+//   U      = k^T (v_new e^{g_last - g_t}) tcgen05 M=128, N=128, K=64
+//   [.; L] = [. ; P] v_new                tcgen05 M=128, N=128, K=64 (rows 64..127)
+//   h_{c+1} = e^{g_last} h_c + U          registers
+//   o_c    = scale (L + e^{g_t} G)        rows t on TMEM lanes 64..127 -> TMA store
 //
-// The epilogue of chunk c-1 runs while the tensor core computes S, X, G of
-// chunk c. Arithmetic matches the separate kernels of the chain: the state is
-// rounded to bf16 only as an MMA operand (as the chain's bf16 h), v_new is
-// rounded to bf16 once (as the chain's stored v_new).
+// w and q of a chunk sit in shared memory as one stacked [w; q] K-major tile,
+// so X and G (and S) are single M=128 products: full-rate tensor-core shapes
+// with half the instructions of two M=64 products, and the state copy is read
+// once. With M=128 accumulators row t lives on TMEM lane t (X) or 64+t (G, S,
+// L), so the math warps split by subpartition: the warps on lanes 0..63 form
+// v_new (the state path) while the warps on lanes 64..127 write the previous
+// chunk's output and form P. Arithmetic matches the separate kernels of the
+// chain: the state is rounded to bf16 only as an MMA operand (as the chain's
+// bf16 h) and v_new once to bf16 (as the chain's stored v_new).
 //
-// TMEM (512 columns): U [0,128) | X/G of chunk parity 0 [128,256) and 1
-// [256,384) (X at lane 0, G at lane 16) | L [384,512) at lane 0, S [384,448)
-// at lane 16. Shared memory: two 64 KB TMA stages (k, q, w, u tiles of a
-// chunk, 128-B swizzle) + state copy 32 KB + v_new 16 KB + P 8 KB + o 16 KB.
+// TMEM (512 columns): U [0,128) | [X; G] of chunk parity 0 [128,256) and 1
+// [256,384) | L [384,512), shared with S [384,448) (S(c+1) is written once the
+// epilogue has read L(c)). Shared memory: two 64 KB TMA stages (k, [w; q], u
+// tiles of a chunk, 128-B swizzle) + state copy 32 KB + v_new 16 KB + [pad; P]
+// 16 KB + o 16 KB.
 #include <cuda_bf16.h>
 
 #include "host_util.h"
@@ -41,34 +47,24 @@ namespace delta_ho {
 constexpr int kBT = 64;
 constexpr int kK = 128;
 constexpr int kV = 128;
-constexpr int kMath = 256;             // math warps: 2 warpgroups
-constexpr int kThreads = kMath + 64;   // + tcgen05 issuer warp + TMA producer warp
-constexpr int kWG = kMath / 128;       // warps sharing a TMEM subpartition
-constexpr int kCW = kV / kWG;          // V columns per math warp
-constexpr int kPW = kBT / kWG;         // P columns per math warp
-
-// 16x256b TMEM load of N/2 8-column groups (N = 2, 4 or 8 registers per group pair).
-template <int N>
-__device__ __forceinline__ void tmem_ld_16x256b(uint32_t taddr, float* v) {
-  if constexpr (N == 8) tmem_ld_16x256b_x8(taddr, v);
-  else if constexpr (N == 4) tmem_ld_16x256b_x4(taddr, v);
-  else tmem_ld_16x256b_x2(taddr, v);
-}
+constexpr int kMath = 256;            // 8 math warps: 4 on TMEM lanes 0..63, 4 on lanes 64..127
+constexpr int kThreads = kMath + 64;  // + tcgen05 issuer warp + TMA producer warp
 
 struct Layout {
   static constexpr int TILE = kBT * 128 * 2;  // [64 x 128] bf16 = two 8 KB boxes
-  static constexpr int OFF_K = 0, OFF_Q = TILE, OFF_W = 2 * TILE, OFF_U = 3 * TILE;
-  static constexpr int STAGE = 4 * TILE;                 // 64 KB
-  static constexpr int OFF_S = 2 * STAGE;                // state copy [128 x 128] bf16, two 16 KB MN blocks
-  static constexpr int OFF_VN = OFF_S + kK * kV * 2;     // v_new [64 x 128] bf16
-  static constexpr int OFF_P = OFF_VN + TILE;            // P [64 x 64] bf16
-  static constexpr int OFF_O = OFF_P + kBT * kBT * 2;    // o staging [64 x 128] bf16
+  static constexpr int OFF_K = 0;              // k: boxes j at +8 KB j
+  static constexpr int OFF_WQ = TILE;          // [w; q]: K-block j at +16 KB j, w rows then q rows
+  static constexpr int OFF_U = 3 * TILE;       // u: boxes j at +8 KB j
+  static constexpr int STAGE = 4 * TILE;       // 64 KB
+  static constexpr int OFF_S = 2 * STAGE;      // state copy [128 x 128] bf16, two 16 KB MN blocks
+  static constexpr int OFF_VN = OFF_S + kK * kV * 2;  // v_new [64 x 128] bf16
+  static constexpr int OFF_P = OFF_VN + TILE;         // [pad 8 KB; P [64 x 64] bf16]
+  static constexpr int OFF_O = OFF_P + 2 * kBT * kBT * 2;  // o staging [64 x 128] bf16
   static constexpr int OFF_MISC = OFF_O + TILE;
-  // misc: sG [2][64] | scale e^{g} [2][64] | barriers, TMEM slot
+  // misc: sG [3][64] | scale e^{g} [2][64] | e^{g_m - g_s} [64] | barriers, TMEM slot
   static constexpr int SMEM = OFF_MISC + 2048 + 1024;
 };
 
-__device__ __forceinline__ uint32_t ld_u32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 __device__ __forceinline__ float2 bf2_to_f2(uint32_t x) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x));
 }
@@ -80,26 +76,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const float* __restrict__ h0, float* __restrict__ final_state, float scale, int T_len,
                           int H) {
   using Ly = Layout;
-  constexpr uint32_t kIdS = make_idesc(1u, 64, 64, 0, 0);
-  constexpr uint32_t kIdXG = make_idesc(1u, 64, kV, 0, 1);
+  constexpr uint32_t kIdXG = make_idesc(1u, 128, kV, 0, 1);
+  constexpr uint32_t kIdS = make_idesc(1u, 128, 64, 0, 0);
   constexpr uint32_t kIdU = make_idesc(1u, kK, kV, 1, 1);
-  constexpr uint32_t kIdL = make_idesc(1u, 64, kV, 0, 1);
+  constexpr uint32_t kIdL = make_idesc(1u, 128, kV, 0, 1);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(sm);
-  float* sG = reinterpret_cast<float*>(sm + Ly::OFF_MISC);           // [2][64]
-  float* sEg = reinterpret_cast<float*>(sm + Ly::OFF_MISC + 512);    // [2][64] scale e^{g_t}
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::OFF_MISC + 1024);
+  float* sG = reinterpret_cast<float*>(sm + Ly::OFF_MISC);           // [3][64] gates, ring
+  float* sEg = reinterpret_cast<float*>(sm + Ly::OFF_MISC + 768);    // [2][64] scale e^{g_t}
+  float* sEb = reinterpret_cast<float*>(sm + Ly::OFF_MISC + 1280);   // [64] e^{g_m - g_s} of the chunk
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::OFF_MISC + 1536);
   uint64_t* full = bars;          // [2] TMA stage landed
   uint64_t* s_ready = bars + 2;   // h_c copied to smem (one arrival per math warp)
-  uint64_t* vn_ready = bars + 3;  // v_new in smem (one arrival per math warp)
-  uint64_t* p_ready = bars + 4;   // P in smem (one arrival per math warp)
-  uint64_t* bar_s = bars + 5;     // S = q k^T in TMEM
-  uint64_t* bar_a = bars + 6;     // X, G in TMEM
-  uint64_t* bar_u = bars + 7;     // U in TMEM (stage consumed)
-  uint64_t* bar_l = bars + 8;     // L in TMEM
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* vn_ready = bars + 3;  // v_new in smem (one arrival per lane-0..63 warp)
+  uint64_t* p_ready = bars + 4;   // P in smem (one arrival per lane-64..127 warp)
+  uint64_t* e_done = bars + 5;    // L of the previous chunk read out (lane-64..127 warps)
+  uint64_t* bar_s = bars + 6;     // S in TMEM
+  uint64_t* bar_a = bars + 7;     // X, G in TMEM
+  uint64_t* bar_u = bars + 8;     // U in TMEM (stage consumed)
+  uint64_t* bar_l = bars + 9;     // L in TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x;
@@ -110,8 +108,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&full[0], 1);
     mbar_init(&full[1], 1);
     mbar_init(s_ready, kMath / 32);
-    mbar_init(vn_ready, kMath / 32);
-    mbar_init(p_ready, kMath / 32);
+    mbar_init(vn_ready, kMath / 64);
+    mbar_init(p_ready, kMath / 64);
+    mbar_init(e_done, kMath / 64);
     mbar_init(bar_s, 1);
     mbar_init(bar_a, 1);
     mbar_init(bar_u, 1);
@@ -126,10 +125,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     sG[tid] = g[(long long)(b * T_len + tid) * H + hh];
     if (NT > 1) sG[64 + tid] = g[(long long)(b * T_len + kBT + tid) * H + hh];
   }
+  if (tid < kMath) {
+    // rows 0..63 of the L product's A operand: never read back, zeroed so the
+    // unused accumulator rows stay finite
+    reinterpret_cast<uint4*>(sm + Ly::OFF_P)[2 * tid] = make_uint4(0, 0, 0, 0);
+    reinterpret_cast<uint4*>(sm + Ly::OFF_P)[2 * tid + 1] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+  }
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t tU = tbase, tL = tbase + 384, tS = tbase + 384 + (16u << 16);
+  const uint32_t tU = tbase, tL = tbase + 384, tS = tbase + 384;
   bool ok = true;
 
   if (warp == kMath / 32 + 1) {
@@ -143,15 +149,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           tma_load_3d(base + Ly::OFF_K + j * 8192, &tm_k, &full[st], j * 64, hh, row0);
-          tma_load_3d(base + Ly::OFF_Q + j * 8192, &tm_q, &full[st], j * 64, hh, row0);
-          tma_load_3d(base + Ly::OFF_W + j * 8192, &tm_w, &full[st], j * 64, hh, row0);
+          tma_load_3d(base + Ly::OFF_WQ + j * 16384, &tm_w, &full[st], j * 64, hh, row0);
+          tma_load_3d(base + Ly::OFF_WQ + j * 16384 + 8192, &tm_q, &full[st], j * 64, hh, row0);
           tma_load_3d(base + Ly::OFF_U + j * 8192, &tm_u, &full[st], j * 64, hh, row0);
         }
       };
       issue_tma(0);
       if (NT > 1) issue_tma(1);
       int issued = NT > 1 ? 2 : 1;
-      // Stage c & 1 is free once U(c) has read it.
+      // Stage c & 1 is free once U(c) -- the last reader of k, w, q, u -- is done.
       for (int c = 0; c + 2 < NT; ++c) {
         if (!mbar_wait(bar_u, c & 1, &g_status_ho)) { ok = false; break; }
         issue_tma(c + 2);
@@ -162,53 +168,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMath / 32) {
     // ---------------- tcgen05 issuer (one thread) ----------------
-    // Per chunk c: X, G | S of chunk c+1 (once P(c) has read S(c)) | U | L.
+    // Per chunk c: [X; G] | S (after the epilogue has read L(c-1)) | U | L.
     if (lane == 0) {
-      auto issue_s = [&](int c) {
-        const uint32_t stg = sbase + (c & 1) * Ly::STAGE;
-#pragma unroll
-        for (int kq = 0; kq < kK / 16; ++kq) {
-          const uint32_t off = (kq / 4) * 8192 + (kq % 4) * 32;
-          mma_bf16_ss(tS, make_sdesc(stg + Ly::OFF_Q + off, 16, 1024), make_sdesc(stg + Ly::OFF_K + off, 16, 1024),
-                      kIdS, kq > 0);
-        }
-        mma_commit(bar_s);
-      };
       uint64_t* last_bar = nullptr;  // last commit, waited (bounded) before TMEM is released
       uint32_t last_ph = 0;
-      if (mbar_wait(&full[0], 0, &g_status_ho)) {
-        tc_fence_after();
-        issue_s(0);
-        last_bar = bar_s;
-      } else {
-        ok = false;
-      }
       for (int c = 0; c < NT && ok; ++c) {
         const int st = c & 1;
         const uint32_t ph = c & 1;
         const uint32_t stg = sbase + st * Ly::STAGE;
         const uint32_t tXG = tbase + 128 + 128 * st;
-        // X = w h_c, G = q h_c (stage c landed: S(c) was issued after its full wait)
-        if (!mbar_wait(s_ready, ph, &g_status_ho)) { ok = false; break; }
+        // [X; G] = [w; q] h_c
+        if (!mbar_wait(&full[st], (c >> 1) & 1, &g_status_ho) || !mbar_wait(s_ready, ph, &g_status_ho)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kq = 0; kq < kK / 16; ++kq)
+          mma_bf16_ss(tXG, make_sdesc(stg + Ly::OFF_WQ + (kq / 4) * 16384 + (kq % 4) * 32, 16, 1024),
+                      make_sdesc(sbase + Ly::OFF_S + kq * 2048, kK * 128, 1024), kIdXG, kq > 0);
+        mma_commit(bar_a);
+        last_bar = bar_a, last_ph = ph;
+        // [.; S] = [w; q] k^T into the L columns, once L(c-1) has been read
+        if (c > 0 && !mbar_wait(e_done, ph ^ 1, &g_status_ho)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kq = 0; kq < kK / 16; ++kq) {
-          const uint32_t off = (kq / 4) * 8192 + (kq % 4) * 32;
-          const uint64_t hd = make_sdesc(sbase + Ly::OFF_S + kq * 2048, kK * 128, 1024);
-          mma_bf16_ss(tXG, make_sdesc(stg + Ly::OFF_W + off, 16, 1024), hd, kIdXG, kq > 0);
-          mma_bf16_ss(tXG + (16u << 16), make_sdesc(stg + Ly::OFF_Q + off, 16, 1024), hd, kIdXG, kq > 0);
+          const uint32_t koff = (kq / 4) * 8192 + (kq % 4) * 32;
+          mma_bf16_ss(tS, make_sdesc(stg + Ly::OFF_WQ + (kq / 4) * 16384 + (kq % 4) * 32, 16, 1024),
+                      make_sdesc(stg + Ly::OFF_K + koff, 16, 1024), kIdS, kq > 0);
         }
-        mma_commit(bar_a);
-        last_bar = bar_a, last_ph = ph;
-        // S of chunk c+1 while the math warps form v_new(c): tS is free once P(c) is in smem.
-        if (!mbar_wait(p_ready, ph, &g_status_ho)) { ok = false; break; }
-        if (c + 1 < NT) {
-          if (!mbar_wait(&full[st ^ 1], ((c + 1) >> 1) & 1, &g_status_ho)) { ok = false; break; }
-          tc_fence_after();
-          issue_s(c + 1);
-          last_bar = bar_s, last_ph = (c + 1) & 1;
-        }
-        // U = k^T (v_new e^{g_last - g_t}), then L = P v_new
+        mma_commit(bar_s);
+        last_bar = bar_s;
+        // U = k^T (v_new e^{g_last - g_t})
         if (!mbar_wait(vn_ready, ph, &g_status_ho)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -216,176 +208,209 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_bf16_ss(tU, make_sdesc(stg + Ly::OFF_K + q * 2048, 8192, 1024),
                       make_sdesc(stg + Ly::OFF_U + q * 2048, 8192, 1024), kIdU, q > 0);
         mma_commit(bar_u);
+        last_bar = bar_u;
+        // [.; L] = [pad; P] v_new (P has read S)
+        if (!mbar_wait(p_ready, ph, &g_status_ho)) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll
         for (int q = 0; q < kBT / 16; ++q)
           mma_bf16_ss(tL, make_sdesc(sbase + Ly::OFF_P + q * 32, 16, 1024),
                       make_sdesc(sbase + Ly::OFF_VN + q * 2048, 8192, 1024), kIdL, q > 0);
         mma_commit(bar_l);
-        last_bar = bar_l, last_ph = ph;
+        last_bar = bar_l;
       }
       // Commits complete in issue order: the last one covers every MMA issued.
       if (last_bar != nullptr) mbar_wait(last_bar, last_ph, &g_status_ho);
     }
   } else {
     // ---------------- math warps ----------------
-    // Warp w reads TMEM lanes 32 (w % 4) ..; the kWG warps of a subpartition
-    // split the 128 V columns (and the 64 P columns) between them.
-    const int sp = warp & 3;
-    const int qc = kCW * (warp >> 2);  // first V column of this warp
-    const int pc = kPW * (warp >> 2);  // first P column of this warp
-    const int kk = tid & 127;          // state row (d) of this thread
+    const int sp = warp & 3;          // TMEM subpartition: lanes 32 sp .. 32 sp + 31
+    const int half = warp >> 2;       // 64-column half of V
+    const int qc = 64 * half;
+    const int kk = tid & 127;         // state row (d) of this thread
     const uint32_t lane_row = (uint32_t)(32 * sp) << 16;
-    const int r0 = 16 * sp + (lane >> 2), r1 = r0 + 8;  // 16x256b rows of M=64 accumulators
-    const int c4 = 2 * (lane & 3);
+    const bool xwarp = sp < 2;        // lanes 0..63: X rows; else G, S, L rows
+    const int t = (32 * sp + lane) & 63;  // chunk row this thread reads from a M=128 accumulator
+    const int gidx = xwarp ? -1 : ((half * 64) + (sp - 2) * 32 + lane);  // index among lane-64..127 warps
 
-    float S[kCW];
+    float S[64];
 #pragma unroll
-    for (int j = 0; j < kCW; ++j) S[j] = 0.f;
+    for (int j = 0; j < 64; ++j) S[j] = 0.f;
     if (h0 != nullptr) {
       const float* src = h0 + (((long long)b * H + hh) * kK + kk) * kV + qc;
 #pragma unroll
-      for (int j = 0; j < kCW; j += 4) {
+      for (int j = 0; j < 64; j += 4) {
         const float4 x = *reinterpret_cast<const float4*>(src + j);
         S[j] = x.x; S[j + 1] = x.y; S[j + 2] = x.z; S[j + 3] = x.w;
       }
     }
 
-    // o tile of chunk j: scale L + scale e^{g_t} G -> staging -> TMA store.
-    // Its first named barrier is also the uniform timeout vote.
-    auto epilogue = [&](int j, bool good) -> bool {
-      if (tid == 0) bulk_wait_group_read0();  // the previous o tile has left the staging buffer
-      if (!named_bar_and(1, kMath, good)) return false;
+    // o of chunk j (lane-64..127 warps): row t, this warp's 64 columns.
+    auto epilogue = [&](int j) {
+      if (gidx == 0) bulk_wait_group_read0();  // the previous o tile has left the staging buffer
+      named_bar_sync(3, kMath / 2);
       tc_fence_after();
-      const float e0 = sEg[(j & 1) * 64 + r0], e1 = sEg[(j & 1) * 64 + r1];
-      uint8_t* ob = sm + Ly::OFF_O;
+      const float e = sEg[(j & 1) * 64 + t];
+      uint8_t* ob = sm + Ly::OFF_O + half * 8192 + t * 128;
 #pragma unroll
-      for (int hq = 0; hq < kCW / 32; ++hq) {  // 32 columns at a time (register pressure)
-        float lv[16], gv[16];
-        tmem_ld_16x256b_x4(tL + lane_row + qc + 32 * hq, lv);
-        tmem_ld_16x256b_x4(tbase + 128 + 128 * (j & 1) + lane_row + (16u << 16) + qc + 32 * hq, gv);
+      for (int hq = 0; hq < 2; ++hq) {
+        float lv[32], gv[32];
+        tmem_ld32(tL + lane_row + qc + 32 * hq, lv);
+        tmem_ld32(tbase + 128 + 128 * (j & 1) + lane_row + qc + 32 * hq, gv);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const int cc = qc + 32 * hq + 8 * q + c4;
-          *reinterpret_cast<uint32_t*>(ob + sw128_offset(r0, cc, kBT, 2)) =
-              pack_bf16x2(fmaf(lv[4 * q], scale, gv[4 * q] * e0), fmaf(lv[4 * q + 1], scale, gv[4 * q + 1] * e0));
-          *reinterpret_cast<uint32_t*>(ob + sw128_offset(r1, cc, kBT, 2)) =
-              pack_bf16x2(fmaf(lv[4 * q + 2], scale, gv[4 * q + 2] * e1), fmaf(lv[4 * q + 3], scale, gv[4 * q + 3] * e1));
+          uint4 p;
+          const float* l8 = lv + 8 * q;
+          const float* g8 = gv + 8 * q;
+          p.x = pack_bf16x2(fmaf(l8[0], scale, g8[0] * e), fmaf(l8[1], scale, g8[1] * e));
+          p.y = pack_bf16x2(fmaf(l8[2], scale, g8[2] * e), fmaf(l8[3], scale, g8[3] * e));
+          p.z = pack_bf16x2(fmaf(l8[4], scale, g8[4] * e), fmaf(l8[5], scale, g8[5] * e));
+          p.w = pack_bf16x2(fmaf(l8[6], scale, g8[6] * e), fmaf(l8[7], scale, g8[7] * e));
+          *reinterpret_cast<uint4*>(ob + ((uint32_t)((4 * hq + q) ^ (t & 7)) << 4)) = p;
         }
       }
       tc_fence_before();
       fence_proxy_async_smem();
-      named_bar_sync(1, kMath);
-      if (tid == 0) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(e_done);  // L(j) read: S of the next chunk may overwrite it
+      named_bar_sync(3, kMath / 2);
+      if (gidx == 0) {
         const int row0 = b * T_len + j * kBT;
         tma_store_3d(&tm_o, sm + Ly::OFF_O, 0, hh, row0);
         tma_store_3d(&tm_o, sm + Ly::OFF_O + 8192, 64, hh, row0);
         bulk_commit_group();
       }
-      return true;
     };
 
     for (int c = 0; c < NT; ++c) {
       const int st = c & 1;
       const uint32_t ph = c & 1;
       uint8_t* stage = sm + st * Ly::STAGE;
-      const float* gc = sG + st * 64;
+      const float* gc = sG + (c % 3) * 64;
       const uint32_t tXG = tbase + 128 + 128 * st;
 
-      // (1) h_c -> shared memory (bf16, MN-major B operand of X and G)
+      // (1) h_c -> shared memory (bf16, MN-major B operand of [X; G])
       {
-        uint8_t* tile = sm + Ly::OFF_S + (qc >> 6) * (kK * 128);
+        uint8_t* tile = sm + Ly::OFF_S + half * (kK * 128);
 #pragma unroll
-        for (int j = 0; j < kCW; j += 8) {
+        for (int j = 0; j < 64; j += 8) {
           uint4 p;
           p.x = pack_bf16x2(S[j], S[j + 1]);
           p.y = pack_bf16x2(S[j + 2], S[j + 3]);
           p.z = pack_bf16x2(S[j + 4], S[j + 5]);
           p.w = pack_bf16x2(S[j + 6], S[j + 7]);
-          *reinterpret_cast<uint4*>(tile + sw128_offset(kk, (qc & 63) + j, kK, 2)) = p;
+          *reinterpret_cast<uint4*>(tile + sw128_offset(kk, j, kK, 2)) = p;
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_ready);  // one arrival per warp
+      if (lane == 0) mbar_arrive(s_ready);
 
-      // (2) epilogue of chunk c-1 while the tensor core computes X, G of chunk c
-      cp_async_wait<0>();  // this chunk's gates have landed (visible after the next barrier)
-      if (c > 0) {
-        ok = mbar_wait(bar_l, (c - 1) & 1, &g_status_ho) && ok;
-        if (!epilogue(c - 1, ok)) { ok = false; break; }
-      } else if (!named_bar_and(1, kMath, ok)) {
-        ok = false;
-        break;
-      }
-      // Gates of chunk c+1 into sG[st^1]: every thread is past chunk c-1, its last reader.
-      if (c >= 1 && c + 1 < NT && tid < kBT)
-        cp_async4(&sG[(st ^ 1) * 64 + tid], g + (long long)(b * T_len + (c + 1) * kBT + tid) * H + hh);
-      cp_async_commit();
       const float gl = gc[kBT - 1];
-      const float g0 = gc[r0], g1 = gc[r1];
-      if (tid < kBT) sEg[st * 64 + tid] = __expf(gc[tid]) * scale;
-
-      // (3) P = tril(S e^{g_t - g_s}) -> smem (this warp: kPW columns), while X, G run
-      ok = mbar_wait(bar_s, ph, &g_status_ho) && ok;
-      tc_fence_after();
-      {
-        float sv[kPW / 2];
-        tmem_ld_16x256b<kPW / 4>(tS + lane_row + pc, sv);
-        uint8_t* pb = sm + Ly::OFF_P;
+      const float g_t = gc[t];
+      if (xwarp) {
+        // (2x) v_new = u - X for row t, this warp's 64 columns
+        if (tid < kBT) sEg[st * 64 + tid] = __expf(gc[tid]) * scale;
+        ok = mbar_wait(bar_a, ph, &g_status_ho) && ok;
+        tc_fence_after();
+        const float d = __expf(gl - g_t);
+        const uint8_t* urow = stage + Ly::OFF_U + half * 8192 + t * 128;
+        uint8_t* uw = stage + Ly::OFF_U + half * 8192 + t * 128;
+        uint8_t* vrow = sm + Ly::OFF_VN + half * 8192 + t * 128;
 #pragma unroll
-        for (int q = 0; q < kPW / 8; ++q) {
-          const int cc = pc + 8 * q + c4;
-          const float gc0 = gc[cc], gc1 = gc[cc + 1];
-          const float p00 = (cc <= r0) ? sv[4 * q] * __expf(g0 - gc0) : 0.f;
-          const float p01 = (cc + 1 <= r0) ? sv[4 * q + 1] * __expf(g0 - gc1) : 0.f;
-          const float p10 = (cc <= r1) ? sv[4 * q + 2] * __expf(g1 - gc0) : 0.f;
-          const float p11 = (cc + 1 <= r1) ? sv[4 * q + 3] * __expf(g1 - gc1) : 0.f;
-          *reinterpret_cast<uint32_t*>(pb + sw128_offset(r0, cc, kBT, 2)) = pack_bf16x2(p00, p01);
-          *reinterpret_cast<uint32_t*>(pb + sw128_offset(r1, cc, kBT, 2)) = pack_bf16x2(p10, p11);
-        }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_ready);  // one arrival per warp
-
-      // (4) v_new = u - X -> smem (this warp: kCW columns)
-      ok = mbar_wait(bar_a, ph, &g_status_ho) && ok;
-      tc_fence_after();
-      {
-        float xv[kCW / 2];
-        tmem_ld_16x256b<kCW / 8>(tXG + lane_row + qc, xv);
-        const float d0 = __expf(gl - g0), d1 = __expf(gl - g1);
-        uint8_t* ut = stage + Ly::OFF_U;
-        uint8_t* vn = sm + Ly::OFF_VN;
+        for (int hq = 0; hq < 2; ++hq) {
+          float xv[32];
+          tmem_ld32(tXG + lane_row + qc + 32 * hq, xv);
 #pragma unroll
-        for (int q = 0; q < kCW / 8; ++q) {
-          const int cc = qc + 8 * q + c4;
-          const uint32_t o0 = sw128_offset(r0, cc, kBT, 2), o1 = sw128_offset(r1, cc, kBT, 2);
-          const float2 u0 = bf2_to_f2(ld_u32(ut + o0)), u1 = bf2_to_f2(ld_u32(ut + o1));
-          const float n00 = u0.x - xv[4 * q], n01 = u0.y - xv[4 * q + 1];
-          const float n10 = u1.x - xv[4 * q + 2], n11 = u1.y - xv[4 * q + 3];
-          // v_new (bf16, B operand of L) and v_new e^{g_last - g_t} (bf16, B operand
-          // of U), each rounded once from the fp32 difference.
-          *reinterpret_cast<uint32_t*>(vn + o0) = pack_bf16x2(n00, n01);
-          *reinterpret_cast<uint32_t*>(vn + o1) = pack_bf16x2(n10, n11);
-          *reinterpret_cast<uint32_t*>(ut + o0) = pack_bf16x2(n00 * d0, n01 * d0);
-          *reinterpret_cast<uint32_t*>(ut + o1) = pack_bf16x2(n10 * d1, n11 * d1);
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t off = (uint32_t)((4 * hq + q) ^ (t & 7)) << 4;
+            const uint4 uu = *reinterpret_cast<const uint4*>(urow + off);
+            const uint32_t uw4[4] = {uu.x, uu.y, uu.z, uu.w};
+            uint32_t vn4[4], us4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 u2 = bf2_to_f2(uw4[e]);
+              const float n0 = u2.x - xv[8 * q + 2 * e], n1 = u2.y - xv[8 * q + 2 * e + 1];
+              // v_new (B operand of L) and v_new e^{g_last - g_t} (B operand of U),
+              // each rounded to bf16 once from the fp32 difference.
+              vn4[e] = pack_bf16x2(n0, n1);
+              us4[e] = pack_bf16x2(n0 * d, n1 * d);
+            }
+            *reinterpret_cast<uint4*>(vrow + off) = make_uint4(vn4[0], vn4[1], vn4[2], vn4[3]);
+            *reinterpret_cast<uint4*>(uw + off) = make_uint4(us4[0], us4[1], us4[2], us4[3]);
+          }
         }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(vn_ready);
+      } else {
+        // (2g) epilogue of chunk c-1, then P(c) = tril(S e^{g_t - g_s}) for row t
+        if (c > 0) {
+          ok = mbar_wait(bar_l, (c - 1) & 1, &g_status_ho) && ok;
+          epilogue(c - 1);
+        }
+        // Decay e^{g_t - g_s} = e^{g_t - g_m} e^{g_m - g_s} about the middle g_m of the
+        // chunk's gate range: 64 + 1 exponentials per chunk instead of one per entry.
+        // Each factor is at most e^{range / 2}; chunks whose gates span more than 120
+        // (factors past e^60) take one exponential per entry instead.
+        float mn = fminf(gc[lane], gc[lane + 32]), mx = fmaxf(gc[lane], gc[lane + 32]);
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) {
+          mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, m));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+        }
+        const bool factored = mx - mn <= 120.f;  // warp-uniform
+        const float gm = 0.5f * (mn + mx);
+        if (gidx < kBT) sEb[gidx] = __expf(gm - gc[gidx]);
+        named_bar_sync(3, kMath / 2);
+        const float a_t = __expf(g_t - gm);
+        ok = mbar_wait(bar_s, ph, &g_status_ho) && ok;
+        tc_fence_after();
+        uint8_t* prow = sm + Ly::OFF_P + 8192 + t * 128;
+        if (half == 1 && t < 32) {
+          // columns 32..63 of rows 0..31 are above the diagonal
+#pragma unroll
+          for (int q = 4; q < 8; ++q) *reinterpret_cast<uint4*>(prow + ((uint32_t)(q ^ (t & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+        } else {
+          float sv[32];
+          tmem_ld32(tS + lane_row + 32 * half, sv);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t p4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int s0 = 32 * half + 8 * q + 2 * e;
+              const float f0 = factored ? a_t * sEb[s0] : __expf(g_t - gc[s0]);
+              const float f1 = factored ? a_t * sEb[s0 + 1] : __expf(g_t - gc[s0 + 1]);
+              const float a = (s0 <= t) ? sv[8 * q + 2 * e] * f0 : 0.f;
+              const float bb = (s0 + 1 <= t) ? sv[8 * q + 2 * e + 1] * f1 : 0.f;
+              p4[e] = pack_bf16x2(a, bb);
+            }
+            *reinterpret_cast<uint4*>(prow + ((uint32_t)((4 * half + q) ^ (t & 7)) << 4)) =
+                make_uint4(p4[0], p4[1], p4[2], p4[3]);
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_ready);
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(vn_ready);  // one arrival per warp
 
-      // (5) h_{c+1} = e^{g_last} h_c + U
+      // (3) h_{c+1} = e^{g_last} h_c + U; all math threads vote (uniform timeout exit)
       ok = mbar_wait(bar_u, ph, &g_status_ho) && ok;
+      cp_async_wait<0>();  // gates of chunk c+1 (issued one iteration ago) have landed
+      if (!named_bar_and(1, kMath, ok)) { ok = false; break; }
+      // Gates of chunk c+2 into ring slot (c+2) % 3: its last readers (chunk c-1) are done.
+      if (c + 2 < NT && tid < kBT)
+        cp_async4(&sG[((c + 2) % 3) * 64 + tid], g + (long long)(b * T_len + (c + 2) * kBT + tid) * H + hh);
+      cp_async_commit();
       tc_fence_after();
       {
         const float eg = __expf(gl);
 #pragma unroll
-        for (int hq = 0; hq < kCW / 32; ++hq) {
+        for (int hq = 0; hq < 2; ++hq) {
           float ur[32];
           tmem_ld32(tU + lane_row + qc + 32 * hq, ur);
 #pragma unroll
@@ -394,14 +419,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
     }
-    if (ok && NT > 0) ok = mbar_wait(bar_l, (NT - 1) & 1, &g_status_ho);
-    if (ok && NT > 0) ok = epilogue(NT - 1, ok);
+    if (ok && NT > 0 && !xwarp) {
+      ok = mbar_wait(bar_l, (NT - 1) & 1, &g_status_ho);
+      epilogue(NT - 1);
+    }
     cp_async_wait<0>();
-    if (tid == 0) bulk_wait_group0();
+    if (gidx == 0) bulk_wait_group0();
     if (ok && final_state != nullptr) {
       float* dst = final_state + (((long long)b * H + hh) * kK + kk) * kV + qc;
 #pragma unroll
-      for (int j = 0; j < kCW; j += 4)
+      for (int j = 0; j < 64; j += 4)
         *reinterpret_cast<float4*>(dst + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
     }
   }
