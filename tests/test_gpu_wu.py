@@ -110,3 +110,22 @@ def test_fused_many_units_per_cta(sign):
         assert_close(A_out[b:b + 1, :, hh:hh + 1].cpu().double(), torch.from_numpy(A), 1e-3, 1e-4, "A")
         assert_close(w[b:b + 1, :, hh:hh + 1].float().cpu().double(), torch.from_numpy(rw), TOL, TOL, "w")
         assert_close(u[b:b + 1, :, hh:hh + 1].float().cpu().double(), torch.from_numpy(ru), TOL, TOL, "u")
+
+
+@pytest.mark.parametrize("sign", [1, -1])
+def test_fused_A_steep_gates(sign):
+    """Chunks whose gates span more than 120 keep one exponential per M entry
+    (the two-factor decay would leave fp32 range); mixed with gentle chunks."""
+    from theorem_b200 import ops
+    B, T, H, K, V = 1, 256, 2, 128, 128
+    d = deltanet_inputs(B, T, H, K, V, seed=60 + sign)
+    gen = torch.Generator().manual_seed(61)
+    inc = -3.0 * torch.rand(B, T, H, generator=gen)
+    inc[:, 64:128] *= 0.01
+    g = inc.reshape(B, T // 64, 64, H).cumsum(2).reshape(B, T, H).contiguous()
+    k, v, beta = d["k"], d["v"], d["beta"]
+    w, u = ops.recompute_w_u(k.to(DEV), v.to(DEV), beta.to(DEV), None, g.to(DEV), a_mode=sign)
+    A = orc.build_A(k.float(), beta, g, sign)
+    rw, ru = orc.recompute_w_u(k.float(), v.float(), beta, A, g)
+    assert_close(w.float().cpu().double(), torch.from_numpy(rw), 2e-2, 2e-2, "w")
+    assert_close(u.float().cpu().double(), torch.from_numpy(ru), 2e-2, 2e-2, "u")

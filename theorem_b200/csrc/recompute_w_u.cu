@@ -419,8 +419,10 @@ struct Layout {
   static constexpr int G_AW = 2 * 64 * LDM * 4;          //   A diag(beta e^g) bf16, K-major
   static constexpr int G_AU = G_AW + 8192;               //   A diag(beta) bf16, K-major
   static constexpr int GRP = G_AU + 8192;
-  static constexpr int OFF_SC = OFF_GRP + 2 * GRP;       // beta, g, beta*e^g [3][3][64] f32
-  static constexpr int OFF_BAR = OFF_SC + kStages * 3 * 64 * 4;
+  static constexpr int SC = 6 * 64;                      // per stage: beta | g | beta e^g |
+                                                         //   beta e^{g - g_m} | e^{g_m - g} | flag
+  static constexpr int OFF_SC = OFF_GRP + 2 * GRP;
+  static constexpr int OFF_BAR = OFF_SC + kStages * SC * 4;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
 };
 
@@ -530,15 +532,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int hh = u % H, bc = u / H, c = bc % NT, b = bc / NT;
       const int row0 = b * T_len + c * 64;
-      float* sc = sSc + st * 192;
+      float* sc = sSc + st * Ly::SC;
+      const long long gi0 = (long long)(row0 + lane) * H + hh, gi1 = gi0 + 32LL * H;
+      const float bv0 = beta[gi0], gv0 = g[gi0], bv1 = beta[gi1], gv1 = g[gi1];
+      // Decay e^{g_r - g_c} = e^{g_r - g_m} e^{g_m - g_c} about the middle g_m of the
+      // chunk's gate range (each factor at most e^{range/2}; ranges over 120 keep one
+      // exponential per entry, flag 0).
+      float mn = fminf(gv0, gv1), mx = fmaxf(gv0, gv1);
 #pragma unroll
-      for (int r = lane; r < 64; r += 32) {
-        const long long gi = (long long)(row0 + r) * H + hh;
-        const float bv = beta[gi], gv = g[gi];
-        sc[r] = bv;
-        sc[64 + r] = gv;
-        sc[128 + r] = bv * __expf(gv);
+      for (int m = 16; m >= 1; m >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, m));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
       }
+      const float gm = 0.5f * (mn + mx);
+      sc[lane] = bv0;
+      sc[32 + lane] = bv1;
+      sc[64 + lane] = gv0;
+      sc[96 + lane] = gv1;
+      sc[128 + lane] = bv0 * __expf(gv0);
+      sc[160 + lane] = bv1 * __expf(gv1);
+      sc[192 + lane] = bv0 * __expf(gv0 - gm);
+      sc[224 + lane] = bv1 * __expf(gv1 - gm);
+      sc[256 + lane] = __expf(gm - gv0);
+      sc[288 + lane] = __expf(gm - gv1);
+      if (lane == 0) sc[320] = (mx - mn <= 120.f) ? 1.f : 0.f;
       if (lane == 0) {
         uint8_t* stg = sm + Ly::OFF_STAGE + st * Ly::STAGE;
         mbar_arrive_expect_tx(&full[st], Ly::STAGE);
@@ -630,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ph = (i >> 1) & 1;
       const int hh = u % H, bc = u / H, c = bc % NT, b = bc / NT;
       const int row0 = b * T_len + c * 64;
-      const float* sc = sSc + st * 192;
+      const float* sc = sSc + st * Ly::SC;
       ok = mbar_wait(&full[st], (i / kStages) & 1, &g_status_wu) && mbar_wait(&kfull[grp], ph, &g_status_wu);
       if (mt == 0) bulk_wait_group_read0();  // the previous w/u tiles have left sM / sA
       if (!named_bar_and(bar_vote, kGroup, ok)) { ok = false; break; }
@@ -643,18 +660,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&tfree_k[grp]);
         const int r0 = 16 * sp + (lane >> 2), r1 = r0 + 8;
         const float b0 = sc[r0], b1 = sc[r1], g0 = sc[64 + r0], g1 = sc[64 + r1];
+        const float fa0 = sc[192 + r0], fa1 = sc[192 + r1];
+        const bool factored = sc[320] != 0.f;  // uniform
         // Only the strictly lower triangle of M is ever read (the solve below and
         // T = M10 A00): this warp's rows 16sp..16sp+15 need column groups j <= 2sp+1.
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if (j > 2 * sp + 1) break;  // warp-uniform
           const int cc = 8 * j + 2 * (lane & 3);
-          const float gc0 = sc[64 + cc], gc1 = sc[64 + cc + 1];
           float2 m0, m1;
-          m0.x = (cc < r0) ? b0 * kv[4 * j] * __expf(g0 - gc0) : 0.f;
-          m0.y = (cc + 1 < r0) ? b0 * kv[4 * j + 1] * __expf(g0 - gc1) : 0.f;
-          m1.x = (cc < r1) ? b1 * kv[4 * j + 2] * __expf(g1 - gc0) : 0.f;
-          m1.y = (cc + 1 < r1) ? b1 * kv[4 * j + 3] * __expf(g1 - gc1) : 0.f;
+          if (factored) {
+            const float fb0 = sc[256 + cc], fb1 = sc[256 + cc + 1];
+            m0.x = (cc < r0) ? fa0 * kv[4 * j] * fb0 : 0.f;
+            m0.y = (cc + 1 < r0) ? fa0 * kv[4 * j + 1] * fb1 : 0.f;
+            m1.x = (cc < r1) ? fa1 * kv[4 * j + 2] * fb0 : 0.f;
+            m1.y = (cc + 1 < r1) ? fa1 * kv[4 * j + 3] * fb1 : 0.f;
+          } else {
+            const float gc0 = sc[64 + cc], gc1 = sc[64 + cc + 1];
+            m0.x = (cc < r0) ? b0 * kv[4 * j] * __expf(g0 - gc0) : 0.f;
+            m0.y = (cc + 1 < r0) ? b0 * kv[4 * j + 1] * __expf(g0 - gc1) : 0.f;
+            m1.x = (cc < r1) ? b1 * kv[4 * j + 2] * __expf(g1 - gc0) : 0.f;
+            m1.y = (cc + 1 < r1) ? b1 * kv[4 * j + 3] * __expf(g1 - gc1) : 0.f;
+          }
           *reinterpret_cast<float2*>(&sM[r0][cc]) = m0;
           *reinterpret_cast<float2*>(&sM[r1][cc]) = m1;
         }
