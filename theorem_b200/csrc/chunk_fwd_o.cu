@@ -1,7 +1,11 @@
 // chunk_fwd_o.cu -- gated-DeltaNet chunkwise output on tcgen05 tensor cores.
 //
 // Replaces kernels/chunk_fwd_o/kernel.py:52-136 (_chunk_fwd_o_kernel) and its
-// launcher :146-212. Per (b, h, chunk c, 64-wide V tile):
+// launcher :146-212. Three kernels: fp32 activations (the reference contract)
+// take the one-CTA-per-tile kernel below; bf16 activations take a persistent
+// warp-specialized kernel, with a bf16 h (ws::) or an fp32 h (ws32::).
+//
+// fp32 kernel, per (b, h, chunk c, 64-wide V tile):
 //
 //   S = q k^T                                (M=64, N=64,  K=K)  tensor core
 //   G = q h[c]                               (M=64, N=VT,  K=K)  tensor core, tf32
@@ -16,12 +20,9 @@
 //
 // Data movement: q, k, v tiles and the fp32 state tile h[c][:, v-tile] arrive
 // by TMA on one mbarrier, already in UMMA canonical layouts: 128-B swizzle
-// (16-B chunks) for K-major and bf16 MN-major tiles, 128-B swizzle with 32-B
-// atoms for the MN-major tf32 tiles (h, and v when fp32); the
-// accumulators live in TMEM (G: VT columns, S then L: 64 columns). q·h runs
-// in kind::tf32 so h is consumed in fp32 straight from HBM; for bf16
-// activations q is widened to fp32 in shared memory first. For fp32
-// activations (the reference contract, fp32 throughout) S and L use 3xTF32
+// (16-B chunks) for K-major tiles, 128-B swizzle with 32-B atoms for the
+// MN-major tf32 tiles (h, v); the accumulators live in TMEM (G: VT columns,
+// S then L: 64 columns). All products run in kind::tf32, S and L as 3xTF32
 // (x = hi + lo, hi = tf32(x): hi*hi + hi*lo + lo*hi), which keeps them at
 // fp32 accuracy; the lo tiles of q and k are reused for lo(P) once S is done.
 #include <cuda_bf16.h>
@@ -38,22 +39,20 @@ constexpr int kThreads = 128;
 constexpr int kBT = 64;  // chunk length
 constexpr int kVT = 64;  // V tile per CTA
 
-template <typename T, int K>
+template <int K>
 struct Layout {
-  static constexpr int ES = sizeof(T);
+  static constexpr int ES = 4;
   static constexpr int Q_BYTES = kBT * K * ES;       // [64 x K]  K-major
   static constexpr int V_BYTES = kBT * kVT * ES;     // [64 x VT] MN-major
   static constexpr int H_BYTES = K * kVT * 4;        // [K x VT]  MN-major fp32
-  static constexpr int QG_BYTES = (ES == 2) ? kBT * K * 4 : 0;  // fp32 copy of q (bf16 path)
   static constexpr int P_BYTES = kBT * kBT * ES;     // [64 x 64] K-major
-  static constexpr int LO_Q = (ES == 4) ? Q_BYTES : 0;  // fp32: lo(q), lo(k), then lo(P)
-  static constexpr int LO_V = (ES == 4) ? V_BYTES : 0;  // fp32: lo(v)
+  static constexpr int LO_Q = Q_BYTES;               // lo(q), lo(k), then lo(P)
+  static constexpr int LO_V = V_BYTES;               // lo(v)
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + Q_BYTES;
   static constexpr int OFF_H = OFF_V + V_BYTES;
-  static constexpr int OFF_QG = OFF_H + H_BYTES;
-  static constexpr int OFF_P = OFF_QG + QG_BYTES;
+  static constexpr int OFF_P = OFF_H + H_BYTES;
   static constexpr int OFF_QLO = OFF_P + P_BYTES;
   static constexpr int OFF_KLO = OFF_QLO + LO_Q;
   static constexpr int OFF_VLO = OFF_KLO + LO_Q;
@@ -65,19 +64,17 @@ struct Layout {
   static constexpr uint32_t TMEM_COLS = 128;  // G [0,64) | S/L [64,128)
 };
 
-template <typename T, int K>
+template <int K>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_fwd_o_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_h,
-                       const float* __restrict__ g, T* __restrict__ o, float scale, int T_len, int H, int V,
+                       const float* __restrict__ g, float* __restrict__ o, float scale, int T_len, int H, int V,
                        int NT) {
-  using Ly = Layout<T, K>;
-  constexpr bool kBf16 = sizeof(T) == 2;
-  constexpr uint32_t kFmt = kBf16 ? 1u : 2u;       // UMMA A/B format of S and L
-  constexpr int kStep = kBf16 ? 16 : 8;            // K per MMA instruction
-  constexpr uint32_t kIdS = make_idesc(kFmt, 64, 64, 0, 0);
+  using Ly = Layout<K>;
+  constexpr int kStep = 8;  // K per tf32 MMA instruction
+  constexpr uint32_t kIdS = make_idesc(2u, 64, 64, 0, 0);
   constexpr uint32_t kIdG = make_idesc(2u, 64, kVT, 0, 1);
-  constexpr uint32_t kIdL = make_idesc(kFmt, 64, kVT, 0, 1);
+  constexpr uint32_t kIdL = make_idesc(2u, 64, kVT, 0, 1);
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -144,30 +141,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   ok = __syncthreads_and(ok);
   if (!ok) goto cleanup_tma;
 
-  if constexpr (!kBf16) {
-    split_tf32_tile(sm + Ly::OFF_Q, sm + Ly::OFF_QLO, Ly::Q_BYTES, tid, kThreads);
-    split_tf32_tile(sm + Ly::OFF_K, sm + Ly::OFF_KLO, Ly::Q_BYTES, tid, kThreads);
-    split_tf32_tile(sm + Ly::OFF_V, sm + Ly::OFF_VLO, Ly::V_BYTES, tid, kThreads);
-    fence_proxy_async_smem();
-    __syncthreads();
-  }
-  if constexpr (kBf16) {
-    // q (bf16, K-major SW128) -> fp32 copy (K-major SW128) for the tf32 q.h MMA.
-    const uint8_t* sq = sm + Ly::OFF_Q;
-    uint8_t* sqg = sm + Ly::OFF_QG;
-    for (int i = tid; i < kBT * K / 8; i += kThreads) {
-      const int t = i / (K / 8);
-      const int k0 = (i % (K / 8)) * 8;
-      const uint4 raw = *reinterpret_cast<const uint4*>(sq + sw128_offset(t, k0, kBT, 2));
-      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-      float2 f0 = __bfloat1622float2(p2[0]), f1 = __bfloat1622float2(p2[1]);
-      float2 f2 = __bfloat1622float2(p2[2]), f3 = __bfloat1622float2(p2[3]);
-      *reinterpret_cast<float4*>(sqg + sw128_offset(t, k0, kBT, 4)) = make_float4(f0.x, f0.y, f1.x, f1.y);
-      *reinterpret_cast<float4*>(sqg + sw128_offset(t, k0 + 4, kBT, 4)) = make_float4(f2.x, f2.y, f3.x, f3.y);
-    }
-    fence_proxy_async_smem();
-    __syncthreads();
-  }
+  split_tf32_tile(sm + Ly::OFF_Q, sm + Ly::OFF_QLO, Ly::Q_BYTES, tid, kThreads);
+  split_tf32_tile(sm + Ly::OFF_K, sm + Ly::OFF_KLO, Ly::Q_BYTES, tid, kThreads);
+  split_tf32_tile(sm + Ly::OFF_V, sm + Ly::OFF_VLO, Ly::V_BYTES, tid, kThreads);
+  fence_proxy_async_smem();
+  __syncthreads();
 
   if (tid == 0) {
     tc_fence_after();
@@ -178,19 +156,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t off = (kb / 128) * (kBT * 128) + (kb % 128);
       const uint64_t qd = make_sdesc(sbase + Ly::OFF_Q + off, 16, 1024);
       const uint64_t kd = make_sdesc(sbase + Ly::OFF_K + off, 16, 1024);
-      mma_kind<kBf16>(tS, qd, kd, kIdS, kk > 0);
-      if constexpr (!kBf16) {
-        mma_tf32_ss(tS, qd, make_sdesc(sbase + Ly::OFF_KLO + off, 16, 1024), kIdS, 1);
-        mma_tf32_ss(tS, make_sdesc(sbase + Ly::OFF_QLO + off, 16, 1024), kd, kIdS, 1);
-      }
+      mma_tf32_ss(tS, qd, kd, kIdS, kk > 0);
+      mma_tf32_ss(tS, qd, make_sdesc(sbase + Ly::OFF_KLO + off, 16, 1024), kIdS, 1);
+      mma_tf32_ss(tS, make_sdesc(sbase + Ly::OFF_QLO + off, 16, 1024), kd, kIdS, 1);
     }
-    // G = q h  (tf32; A = q in fp32, B = h MN-major)
-    constexpr uint32_t kQgOff = kBf16 ? Ly::OFF_QG : Ly::OFF_Q;
+    // G = q h  (tf32; A = q, B = h MN-major)
 #pragma unroll
     for (int kk = 0; kk < K / 8; ++kk) {
       const uint32_t kb = kk * 32;
       const uint32_t offa = (kb / 128) * (kBT * 128) + (kb % 128);
-      mma_tf32_ss(tG, make_sdesc(sbase + kQgOff + offa, 16, 1024),
+      mma_tf32_ss(tG, make_sdesc(sbase + Ly::OFF_Q + offa, 16, 1024),
                   make_sdesc(sbase + Ly::OFF_H + kk * 8 * 128, K * 128, 512, kSw128Base32), kIdG, kk > 0);
     }
     mma_commit(bar_mma);
@@ -220,26 +195,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = s0 + j;
           pv[j] = (s <= t) ? srow[s] * __expf(gt - sG[s]) : 0.0f;
         }
-        if constexpr (kBf16) {
-          uint4 r;
-          r.x = pack_bf16x2(pv[0], pv[1]);
-          r.y = pack_bf16x2(pv[2], pv[3]);
-          r.z = pack_bf16x2(pv[4], pv[5]);
-          r.w = pack_bf16x2(pv[6], pv[7]);
-          *reinterpret_cast<uint4*>(sp + sw128_offset(t, s0, kBT, 2)) = r;
-        } else {
-          float hi[8], lo[8];
+        float hi[8], lo[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            hi[j] = tf32_round(pv[j]);
-            lo[j] = pv[j] - hi[j];
-          }
-          uint8_t* spl = sm + Ly::OFF_PLO;
-          *reinterpret_cast<float4*>(sp + sw128_offset(t, s0, kBT, 4)) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-          *reinterpret_cast<float4*>(sp + sw128_offset(t, s0 + 4, kBT, 4)) = make_float4(hi[4], hi[5], hi[6], hi[7]);
-          *reinterpret_cast<float4*>(spl + sw128_offset(t, s0, kBT, 4)) = make_float4(lo[0], lo[1], lo[2], lo[3]);
-          *reinterpret_cast<float4*>(spl + sw128_offset(t, s0 + 4, kBT, 4)) = make_float4(lo[4], lo[5], lo[6], lo[7]);
+        for (int j = 0; j < 8; ++j) {
+          hi[j] = tf32_round(pv[j]);
+          lo[j] = pv[j] - hi[j];
         }
+        uint8_t* spl = sm + Ly::OFF_PLO;
+        *reinterpret_cast<float4*>(sp + sw128_offset(t, s0, kBT, 4)) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<float4*>(sp + sw128_offset(t, s0 + 4, kBT, 4)) = make_float4(hi[4], hi[5], hi[6], hi[7]);
+        *reinterpret_cast<float4*>(spl + sw128_offset(t, s0, kBT, 4)) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<float4*>(spl + sw128_offset(t, s0 + 4, kBT, 4)) = make_float4(lo[4], lo[5], lo[6], lo[7]);
       }
     }
   }
@@ -255,15 +221,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t kb = kk * 32;
       const uint32_t offa = (kb / 128) * (kBT * 128) + (kb % 128);
       const uint64_t ad = make_sdesc(sbase + Ly::OFF_P + offa, 16, 1024);
-      if constexpr (kBf16) {
-        mma_bf16_ss(tS, ad, make_sdesc(sbase + Ly::OFF_V + kk * kStep * 128, kBT * 128, 1024, kSw128), kIdL, kk > 0);
-      } else {
-        const uint64_t vd = make_sdesc(sbase + Ly::OFF_V + kk * kStep * 128, kBT * 128, 512, kSw128Base32);
-        const uint64_t vl = make_sdesc(sbase + Ly::OFF_VLO + kk * kStep * 128, kBT * 128, 512, kSw128Base32);
-        mma_tf32_ss(tS, ad, vd, kIdL, kk > 0);
-        mma_tf32_ss(tS, ad, vl, kIdL, 1);
-        mma_tf32_ss(tS, make_sdesc(sbase + Ly::OFF_PLO + offa, 16, 1024), vd, kIdL, 1);
-      }
+      const uint64_t vd = make_sdesc(sbase + Ly::OFF_V + kk * kStep * 128, kBT * 128, 512, kSw128Base32);
+      const uint64_t vl = make_sdesc(sbase + Ly::OFF_VLO + kk * kStep * 128, kBT * 128, 512, kSw128Base32);
+      mma_tf32_ss(tS, ad, vd, kIdL, kk > 0);
+      mma_tf32_ss(tS, ad, vl, kIdL, 1);
+      mma_tf32_ss(tS, make_sdesc(sbase + Ly::OFF_PLO + offa, 16, 1024), vd, kIdL, 1);
     }
     mma_commit(bar_mma);
   }
@@ -277,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = warp * 16 + lane;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     const float eg = (lane < 16) ? sEG[t] * scale : 0.f;
-    T* orow = o + ((long long)(row0 + (lane < 16 ? t : 0)) * H + h) * V + v0;
+    float* orow = o + ((long long)(row0 + (lane < 16 ? t : 0)) * H + h) * V + v0;
 #pragma unroll
     for (int j = 0; j < kVT / 16; ++j) {
       float lv[16], gv[16];
@@ -288,19 +250,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         float r[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) r[i] = fmaf(lv[i], scale, gv[i] * eg);
-        if constexpr (kBf16) {
-          uint4 a, bq;
-          a.x = pack_bf16x2(r[0], r[1]);   a.y = pack_bf16x2(r[2], r[3]);
-          a.z = pack_bf16x2(r[4], r[5]);   a.w = pack_bf16x2(r[6], r[7]);
-          bq.x = pack_bf16x2(r[8], r[9]);  bq.y = pack_bf16x2(r[10], r[11]);
-          bq.z = pack_bf16x2(r[12], r[13]); bq.w = pack_bf16x2(r[14], r[15]);
-          *reinterpret_cast<uint4*>(orow + j * 16) = a;
-          *reinterpret_cast<uint4*>(orow + j * 16 + 8) = bq;
-        } else {
 #pragma unroll
-          for (int i = 0; i < 16; i += 4)
-            *reinterpret_cast<float4*>(orow + j * 16 + i) = make_float4(r[i], r[i + 1], r[i + 2], r[i + 3]);
-        }
+        for (int i = 0; i < 16; i += 4)
+          *reinterpret_cast<float4*>(orow + j * 16 + i) = make_float4(r[i], r[i + 1], r[i + 2], r[i + 3]);
       }
     }
   }
@@ -323,44 +275,40 @@ cleanup_tma:
   if (warp == 0) tmem_dealloc(tbase, Ly::TMEM_COLS);
 }
 
-template <typename T, int K>
+template <int K>
 int launch(const void* q, const void* k, const void* v, const float* g, const float* hst, void* o, float scale,
            int B, int T_len, int H, int V, cudaStream_t st) {
-  using Ly = Layout<T, K>;
-  const CUtensorMapDataType dt = sizeof(T) == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  const int es = sizeof(T);
+  using Ly = Layout<K>;
+  const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   const int NT = T_len / kBT;
   CUtensorMap tq, tk, tv, th;
   const uint64_t rows = (uint64_t)B * T_len;
+  const uint32_t box[3] = {32u, 1u, (uint32_t)kBT};  // 128-B rows of fp32
   {
     uint64_t dims[3] = {(uint64_t)K, (uint64_t)H, rows};
-    uint64_t str[2] = {(uint64_t)K * es, (uint64_t)H * K * es};
-    uint32_t box[3] = {(uint32_t)(128 / es), 1u, (uint32_t)kBT};
+    uint64_t str[2] = {(uint64_t)K * 4, (uint64_t)H * K * 4};
     int r = encode_tiled(&tq, dt, 3, q, dims, str, box);
     if (r == THM_OK) r = encode_tiled(&tk, dt, 3, k, dims, str, box);
     if (r != THM_OK) return r;
   }
   {
     uint64_t dims[3] = {(uint64_t)V, (uint64_t)H, rows};
-    uint64_t str[2] = {(uint64_t)V * es, (uint64_t)H * V * es};
-    uint32_t box[3] = {(uint32_t)(128 / es), 1u, (uint32_t)kBT};
-    int r = encode_tiled(&tv, dt, 3, v, dims, str, box,
-                         es == 2 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    uint64_t str[2] = {(uint64_t)V * 4, (uint64_t)H * V * 4};
+    int r = encode_tiled(&tv, dt, 3, v, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (r != THM_OK) return r;
   }
   {
     uint64_t dims[2] = {(uint64_t)V, (uint64_t)B * NT * H * K};
     uint64_t str[1] = {(uint64_t)V * 4};
-    uint32_t box[2] = {32u, (uint32_t)K};
-    int r = encode_tiled(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, hst, dims, str, box,
-                         CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    uint32_t hbox[2] = {32u, (uint32_t)K};
+    int r = encode_tiled(&th, dt, 2, hst, dims, str, hbox, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (r != THM_OK) return r;
   }
-  auto kern = chunk_fwd_o_kernel<T, K>;
+  auto kern = chunk_fwd_o_kernel<K>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
     return THM_ERR_CUDA;
   dim3 grid(V / kVT, NT, B * H);
-  kern<<<grid, kThreads, Ly::SMEM, st>>>(tq, tk, tv, th, g, static_cast<T*>(o), scale, T_len, H, V, NT);
+  kern<<<grid, kThreads, Ly::SMEM, st>>>(tq, tk, tv, th, g, static_cast<float*>(o), scale, T_len, H, V, NT);
   return check_launch();
 }
 
@@ -1011,6 +959,6 @@ extern "C" int thm_chunk_fwd_o_fwd(const void* q, const void* k, const void* v, 
     return K == 64 ? chunk_o::ws32::launch<64>(q, k, v, g, hf, o, scale, B, T, H, V, st)
                    : chunk_o::ws32::launch<128>(q, k, v, g, hf, o, scale, B, T, H, V, st);
   }
-  return K == 64 ? chunk_o::launch<float, 64>(q, k, v, g, hf, o, scale, B, T, H, V, st)
-                 : chunk_o::launch<float, 128>(q, k, v, g, hf, o, scale, B, T, H, V, st);
+  return K == 64 ? chunk_o::launch<64>(q, k, v, g, hf, o, scale, B, T, H, V, st)
+                 : chunk_o::launch<128>(q, k, v, g, hf, o, scale, B, T, H, V, st);
 }
