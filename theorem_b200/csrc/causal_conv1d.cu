@@ -374,7 +374,7 @@ constexpr int kThreads = 256;
 constexpr int kCh = 256;     // channels per CTA
 constexpr int kRows = 32;    // output rows per tile
 constexpr int kStrip = 256;  // rows per CTA
-constexpr int kStages = 3;
+constexpr int kStages = 2;
 
 template <typename T, int W>
 struct Layout {
@@ -422,7 +422,7 @@ __device__ __forceinline__ float silu_tanh(float x) {
 }
 
 template <typename T, int W, bool SILU, int GL>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 3)
     conv_bsd_tma(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_o,
                  const float* __restrict__ w, const float* __restrict__ bias, int S, int D) {
   using Ly = Layout<T, W>;
