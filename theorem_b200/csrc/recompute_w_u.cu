@@ -641,6 +641,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     float(*sA)[Ly::LDM] = reinterpret_cast<float(*)[Ly::LDM]>(gb + Ly::G_A);
     int prev_hh = 0, prev_row0 = 0;
     bool has_prev = false;
+    {
+      // Rows 0..31, columns 32..63 of A are zero and never rewritten: zero them in
+      // both bf16 operand tiles once (made visible to the tensor core by the fence
+      // before the first afull arrival).
+      const int r = mt >> 2, ck = 4 + (mt & 3);
+      const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(ck ^ (r & 7)) << 4);
+      *reinterpret_cast<uint4*>(gb + Ly::G_AW + off) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(gb + Ly::G_AU + off) = make_uint4(0, 0, 0, 0);
+    }
+    // Converts 8 consecutive entries of a row of A (fp32, columns c0..c0+7, already
+    // masked) into the two column-scaled bf16 MMA operands (and the optional fp32 A).
+    auto put_a8 = [&](const float* a, int t, int c0, const float* sc, int hh, int row0) {
+      const float* fk = sc + 128 + c0;
+      const float* fb = sc + c0;
+      uint4 pw, pu;
+      pw.x = pack_bf16x2(a[0] * fk[0], a[1] * fk[1]); pw.y = pack_bf16x2(a[2] * fk[2], a[3] * fk[3]);
+      pw.z = pack_bf16x2(a[4] * fk[4], a[5] * fk[5]); pw.w = pack_bf16x2(a[6] * fk[6], a[7] * fk[7]);
+      pu.x = pack_bf16x2(a[0] * fb[0], a[1] * fb[1]); pu.y = pack_bf16x2(a[2] * fb[2], a[3] * fb[3]);
+      pu.z = pack_bf16x2(a[4] * fb[4], a[5] * fb[5]); pu.w = pack_bf16x2(a[6] * fb[6], a[7] * fb[7]);
+      *reinterpret_cast<uint4*>(gb + Ly::G_AW + sw128_offset(t, c0, 64, 2)) = pw;
+      *reinterpret_cast<uint4*>(gb + Ly::G_AU + sw128_offset(t, c0, 64, 2)) = pu;
+      if (a_out != nullptr) {
+        float* dst = a_out + ((long long)(row0 + t) * H + hh) * 64 + c0;
+        *reinterpret_cast<float4*>(dst) = make_float4(a[0], a[1], a[2], a[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(a[4], a[5], a[6], a[7]);
+      }
+    };
     for (int i = grp; i < n_local; i += 2) {
       const int u = blockIdx.x + i * gridDim.x;
       const int st = i % kStages;
@@ -649,7 +676,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = b * T_len + c * 64;
       const float* sc = sSc + st * Ly::SC;
       ok = mbar_wait(&full[st], (i / kStages) & 1, &g_status_wu) && mbar_wait(&kfull[grp], ph, &g_status_wu);
-      if (mt == 0) bulk_wait_group_read0();  // the previous w/u tiles have left sM / sA
       if (!named_bar_and(bar_vote, kGroup, ok)) { ok = false; break; }
       tc_fence_after();
       {
@@ -664,26 +690,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool factored = sc[320] != 0.f;  // uniform
         // Only the strictly lower triangle of M is ever read (the solve below and
         // T = M10 A00): this warp's rows 16sp..16sp+15 need column groups j <= 2sp+1.
+        float2 m0[8], m1[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if (j > 2 * sp + 1) break;  // warp-uniform
           const int cc = 8 * j + 2 * (lane & 3);
-          float2 m0, m1;
           if (factored) {
             const float fb0 = sc[256 + cc], fb1 = sc[256 + cc + 1];
-            m0.x = (cc < r0) ? fa0 * kv[4 * j] * fb0 : 0.f;
-            m0.y = (cc + 1 < r0) ? fa0 * kv[4 * j + 1] * fb1 : 0.f;
-            m1.x = (cc < r1) ? fa1 * kv[4 * j + 2] * fb0 : 0.f;
-            m1.y = (cc + 1 < r1) ? fa1 * kv[4 * j + 3] * fb1 : 0.f;
+            m0[j].x = (cc < r0) ? fa0 * kv[4 * j] * fb0 : 0.f;
+            m0[j].y = (cc + 1 < r0) ? fa0 * kv[4 * j + 1] * fb1 : 0.f;
+            m1[j].x = (cc < r1) ? fa1 * kv[4 * j + 2] * fb0 : 0.f;
+            m1[j].y = (cc + 1 < r1) ? fa1 * kv[4 * j + 3] * fb1 : 0.f;
           } else {
             const float gc0 = sc[64 + cc], gc1 = sc[64 + cc + 1];
-            m0.x = (cc < r0) ? b0 * kv[4 * j] * __expf(g0 - gc0) : 0.f;
-            m0.y = (cc + 1 < r0) ? b0 * kv[4 * j + 1] * __expf(g0 - gc1) : 0.f;
-            m1.x = (cc < r1) ? b1 * kv[4 * j + 2] * __expf(g1 - gc0) : 0.f;
-            m1.y = (cc + 1 < r1) ? b1 * kv[4 * j + 3] * __expf(g1 - gc1) : 0.f;
+            m0[j].x = (cc < r0) ? b0 * kv[4 * j] * __expf(g0 - gc0) : 0.f;
+            m0[j].y = (cc + 1 < r0) ? b0 * kv[4 * j + 1] * __expf(g0 - gc1) : 0.f;
+            m1[j].x = (cc < r1) ? b1 * kv[4 * j + 2] * __expf(g1 - gc0) : 0.f;
+            m1[j].y = (cc + 1 < r1) ? b1 * kv[4 * j + 3] * __expf(g1 - gc1) : 0.f;
           }
-          *reinterpret_cast<float2*>(&sM[r0][cc]) = m0;
-          *reinterpret_cast<float2*>(&sM[r1][cc]) = m1;
+        }
+        // the previous unit's w/u tiles (staged in sM / sA) have left shared memory:
+        // waited only now, so the TMA store drains while KK^T is read and scaled
+        if (mt == 0) bulk_wait_group_read0();
+        named_bar_sync(bar_sync, kGroup);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (j > 2 * sp + 1) break;
+          const int cc = 8 * j + 2 * (lane & 3);
+          *reinterpret_cast<float2*>(&sM[r0][cc]) = m0[j];
+          *reinterpret_cast<float2*>(&sM[r1][cc]) = m1[j];
         }
       }
       named_bar_sync(bar_sync, kGroup);
@@ -738,9 +773,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<float4*>(&sA[base + 16 + r][base + c4]) =
             make_float4(-sgn * a4[0], -sgn * a4[1], -sgn * a4[2], -sgn * a4[3]);
       }
-      named_bar_sync(bar_sync, kGroup);
-      // (2) T = M10 A00 (into the M00 corner of sM)
+      // the previous unit's W/U products have consumed the A operand tiles
+      ok = !has_prev || mbar_wait(&ofull[grp], ph ^ 1, &g_status_wu);
+      if (!named_bar_and(bar_vote, kGroup, ok)) { ok = false; break; }
+      // (2) T = M10 A00 (into the M00 corner of sM). Alongside: the diagonal
+      //     32-blocks A00, A11 are final, so their operand entries are written now
+      //     (thread: block mt/64, row (mt/2)%32, 16 columns).
       const int tr = mt >> 2, tc0 = (mt & 3) * 8;
+      {
+        const int blk = mt >> 6, rr = (mt >> 1) & 31, cb0 = (mt & 1) * 16;
+        const int t = 32 * blk + rr;
+#pragma unroll
+        for (int q = 0; q < 16; q += 8) {
+          float a[8];
+          *reinterpret_cast<float4*>(a) = *reinterpret_cast<const float4*>(&sA[t][32 * blk + cb0 + q]);
+          *reinterpret_cast<float4*>(a + 4) = *reinterpret_cast<const float4*>(&sA[t][32 * blk + cb0 + q + 4]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a[e] = (cb0 + q + e <= rr) ? a[e] : 0.f;  // upper triangle unwritten
+          put_a8(a, t, 32 * blk + cb0 + q, sc, hh, row0);
+        }
+        if (blk == 0 && a_out != nullptr) {
+          // the zero block (rows 0..31, columns 32..63) of the fp32 A
+          float* dst = a_out + ((long long)(row0 + t) * H + hh) * 64 + 32 + cb0;
+#pragma unroll
+          for (int q = 0; q < 16; q += 4) *reinterpret_cast<float4*>(dst + q) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
       {
         float t8[8];
 #pragma unroll
@@ -777,41 +835,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           a8[4] = fmaf(av, t1.x, a8[4]); a8[5] = fmaf(av, t1.y, a8[5]);
           a8[6] = fmaf(av, t1.z, a8[6]); a8[7] = fmaf(av, t1.w, a8[7]);
         }
-        *reinterpret_cast<float4*>(&sA[32 + tr][tc0]) =
-            make_float4(-sgn * a8[0], -sgn * a8[1], -sgn * a8[2], -sgn * a8[3]);
-        *reinterpret_cast<float4*>(&sA[32 + tr][tc0 + 4]) =
-            make_float4(-sgn * a8[4], -sgn * a8[5], -sgn * a8[6], -sgn * a8[7]);
-      }
-      // the previous unit's W/U products have consumed the A operands
-      ok = !has_prev || mbar_wait(&ofull[grp], ph ^ 1, &g_status_wu);
-      if (!named_bar_and(bar_vote, kGroup, ok)) { ok = false; break; }
-      // (4) the MMA operands A diag(beta e^g), A diag(beta) in bf16 (+ optional fp32 A)
-      {
-        const int t = mt >> 1, s0 = (mt & 1) * 32;
-        uint8_t* aw = gb + Ly::G_AW;
-        uint8_t* au = gb + Ly::G_AU;
+        // A10 is final here: straight into the operand tiles (no shared-memory copy)
 #pragma unroll
-        for (int q = 0; q < 32; q += 8) {
-          float a[8];
-          *reinterpret_cast<float4*>(a) = *reinterpret_cast<const float4*>(&sA[t][s0 + q]);
-          *reinterpret_cast<float4*>(a + 4) = *reinterpret_cast<const float4*>(&sA[t][s0 + q + 4]);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) a[e] = (s0 + q + e <= t) ? a[e] : 0.f;  // upper triangle unwritten
-          uint4 pw, pu;
-          const float* fk = sc + 128 + s0 + q;
-          const float* fb = sc + s0 + q;
-          pw.x = pack_bf16x2(a[0] * fk[0], a[1] * fk[1]); pw.y = pack_bf16x2(a[2] * fk[2], a[3] * fk[3]);
-          pw.z = pack_bf16x2(a[4] * fk[4], a[5] * fk[5]); pw.w = pack_bf16x2(a[6] * fk[6], a[7] * fk[7]);
-          pu.x = pack_bf16x2(a[0] * fb[0], a[1] * fb[1]); pu.y = pack_bf16x2(a[2] * fb[2], a[3] * fb[3]);
-          pu.z = pack_bf16x2(a[4] * fb[4], a[5] * fb[5]); pu.w = pack_bf16x2(a[6] * fb[6], a[7] * fb[7]);
-          *reinterpret_cast<uint4*>(aw + sw128_offset(t, s0 + q, 64, 2)) = pw;
-          *reinterpret_cast<uint4*>(au + sw128_offset(t, s0 + q, 64, 2)) = pu;
-          if (a_out != nullptr) {
-            float* dst = a_out + ((long long)(row0 + t) * H + hh) * 64 + s0 + q;
-            *reinterpret_cast<float4*>(dst) = make_float4(a[0], a[1], a[2], a[3]);
-            *reinterpret_cast<float4*>(dst + 4) = make_float4(a[4], a[5], a[6], a[7]);
-          }
-        }
+        for (int q = 0; q < 8; ++q) a8[q] *= -sgn;
+        put_a8(a8, 32 + tr, tc0, sc, hh, row0);
       }
       fence_proxy_async_smem();
       mbar_arrive(&afull[grp]);
