@@ -427,26 +427,7 @@ struct Layout {
 };
 
 // W (lane 0) and U (lane 16) are M=64 accumulators interleaved in the same
-// TMEM columns; the 16x256b shape gives each thread rows r0 = 16 sp + lane/4
-// and r0 + 8 with column pairs, packed to bf16x2 in the row-major staging tiles.
-template <int N>
-__device__ __forceinline__ void stage_rows_16x256b(uint32_t taddr, uint8_t* stage, int sp, int lane) {
-  const int r0 = 16 * sp + (lane >> 2), r1 = r0 + 8;
-  const uint32_t sw = (uint32_t)((lane >> 2) & 7);
-#pragma unroll
-  for (int half = 0; half < N / 64; ++half) {
-    float v[32];
-    tmem_ld_16x256b_x8(taddr + 64 * half, v);
-    uint8_t* box = stage + half * 8192;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t off = (((uint32_t)j ^ sw) << 4) + (uint32_t)(lane & 3) * 4;
-      *reinterpret_cast<uint32_t*>(box + r0 * 128 + off) = pack_bf16x2(v[4 * j], v[4 * j + 1]);
-      *reinterpret_cast<uint32_t*>(box + r1 * 128 + off) = pack_bf16x2(v[4 * j + 2], v[4 * j + 3]);
-    }
-  }
-}
-
+// TMEM columns; the epilogue reads both with one 32x32b load per 32 columns.
 template <int K, int V>
 __device__ __forceinline__ void wu_epilogue(uint8_t* gb, uint32_t tbase, int grp, int sp, int lane, int mt,
                                             uint64_t* tfree_o, const CUtensorMap* tm_w, const CUtensorMap* tm_u,
@@ -455,8 +436,31 @@ __device__ __forceinline__ void wu_epilogue(uint8_t* gb, uint32_t tbase, int grp
   const uint32_t tW = tbase + 256 * grp + 64 + ((uint32_t)(32 * sp) << 16);
   uint8_t* ws_ = gb + Ly::G_M;
   uint8_t* us_ = gb + Ly::G_A;
-  stage_rows_16x256b<K>(tW, ws_, sp, lane);
-  stage_rows_16x256b<V>(tW + (16u << 16), us_, sp, lane);
+  // 32x32b loads: TMEM lane 32 sp + l holds W row 16 sp + l (l < 16) or U row
+  // 16 sp + l - 16 (l >= 16), 32 consecutive columns per load; each thread packs
+  // its row into 16-B chunks of the row-major, 128-B-swizzled staging tiles.
+  {
+    const bool is_w = lane < 16;
+    const int r = 16 * sp + (lane & 15);
+    uint8_t* dst = is_w ? ws_ : us_;
+    const int ncol = is_w ? K : V;
+    constexpr int NMAX = K > V ? K : V;
+#pragma unroll
+    for (int c0 = 0; c0 < NMAX; c0 += 32) {
+      float v[32];
+      tmem_ld32(tW + c0, v);
+      if (c0 < ncol) {
+        uint8_t* box = dst + (c0 / 64) * 8192 + r * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t ck = (uint32_t)(((c0 % 64) / 8 + q) ^ (r & 7));
+          *reinterpret_cast<uint4*>(box + (ck << 4)) =
+              make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                         pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+        }
+      }
+    }
+  }
   tc_fence_before();
   mbar_arrive(&tfree_o[grp]);
   fence_proxy_async_smem();
