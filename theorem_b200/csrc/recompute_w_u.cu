@@ -527,9 +527,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
+    // beta, g of unit i are loaded one unit ahead (their latency overlaps the
+    // wait for the stage); row r of a unit at (row0 + r) * H + hh.
+    auto gate_index = [&](int i) {
+      const int u = blockIdx.x + i * gridDim.x;
+      const int hh = u % H, bc = u / H, c = bc % NT, b = bc / NT;
+      return (long long)(b * T_len + c * 64 + lane) * H + hh;
+    };
+    float nb0 = 0.f, ng0 = 0.f, nb1 = 0.f, ng1 = 0.f;
+    if (n_local > 0) {
+      const long long gi = gate_index(0);
+      nb0 = beta[gi]; ng0 = g[gi]; nb1 = beta[gi + 32LL * H]; ng1 = g[gi + 32LL * H];
+    }
     for (int i = 0; i < n_local; ++i) {
       const int u = blockIdx.x + i * gridDim.x;
       const int st = i % kStages;
+      const float bv0 = nb0, gv0 = ng0, bv1 = nb1, gv1 = ng1;
+      if (i + 1 < n_local) {
+        const long long gi = gate_index(i + 1);
+        nb0 = beta[gi]; ng0 = g[gi]; nb1 = beta[gi + 32LL * H]; ng1 = g[gi + 32LL * H];
+      }
       if (i >= kStages) {
         ok = __all_sync(0xffffffffu, mbar_wait(&empty[st], ((i / kStages) & 1) ^ 1, &g_status_wu));
         if (!ok) break;
@@ -537,8 +554,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int hh = u % H, bc = u / H, c = bc % NT, b = bc / NT;
       const int row0 = b * T_len + c * 64;
       float* sc = sSc + st * Ly::SC;
-      const long long gi0 = (long long)(row0 + lane) * H + hh, gi1 = gi0 + 32LL * H;
-      const float bv0 = beta[gi0], gv0 = g[gi0], bv1 = beta[gi1], gv1 = g[gi1];
+      if (lane == 0) {
+        uint8_t* stg = sm + Ly::OFF_STAGE + st * Ly::STAGE;
+        mbar_arrive_expect_tx(&full[st], Ly::STAGE);
+#pragma unroll
+        for (int j = 0; j < K / 64; ++j) tma_load_3d(stg + j * 8192, &tm_k, &full[st], j * 64, hh, row0);
+#pragma unroll
+        for (int j = 0; j < V / 64; ++j) tma_load_3d(stg + Ly::KB + j * 8192, &tm_v, &full[st], j * 64, hh, row0);
+      }
       // Decay e^{g_r - g_c} = e^{g_r - g_m} e^{g_m - g_c} about the middle g_m of the
       // chunk's gate range (each factor at most e^{range/2}; ranges over 120 keep one
       // exponential per entry, flag 0).
@@ -560,14 +583,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       sc[256 + lane] = __expf(gm - gv0);
       sc[288 + lane] = __expf(gm - gv1);
       if (lane == 0) sc[320] = (mx - mn <= 120.f) ? 1.f : 0.f;
-      if (lane == 0) {
-        uint8_t* stg = sm + Ly::OFF_STAGE + st * Ly::STAGE;
-        mbar_arrive_expect_tx(&full[st], Ly::STAGE);
-#pragma unroll
-        for (int j = 0; j < K / 64; ++j) tma_load_3d(stg + j * 8192, &tm_k, &full[st], j * 64, hh, row0);
-#pragma unroll
-        for (int j = 0; j < V / 64; ++j) tma_load_3d(stg + Ly::KB + j * 8192, &tm_v, &full[st], j * 64, hh, row0);
-      }
       mbar_arrive(&full[st]);
     }
   } else if (warp == 1) {
