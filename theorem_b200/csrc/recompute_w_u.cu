@@ -795,7 +795,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the previous unit's W/U products have consumed the A operand tiles
       ok = !has_prev || mbar_wait(&ofull[grp], ph ^ 1, &g_status_wu);
       if (!named_bar_and(bar_vote, kGroup, ok)) { ok = false; break; }
-      // (2) T = M10 A00 (into the M00 corner of sM). Alongside: the diagonal
+      // (2) T = M10 A00, written into the A10 slot of sA (A10 itself goes straight to
+      //     the operand tiles, so the slot is free and nothing in this phase reads
+      //     it: no barrier between the products and the write). Alongside: the diagonal
       //     32-blocks A00, A11 are final, so their operand entries are written now
       //     (thread: block mt/64, row (mt/2)%32, 16 columns).
       const int tr = mt >> 2, tc0 = (mt & 3) * 8;
@@ -833,9 +835,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           t8[4] = fmaf(mv, a1.x, t8[4]); t8[5] = fmaf(mv, a1.y, t8[5]);
           t8[6] = fmaf(mv, a1.z, t8[6]); t8[7] = fmaf(mv, a1.w, t8[7]);
         }
-        named_bar_sync(bar_sync, kGroup);  // everyone done reading M00 / A00
-        *reinterpret_cast<float4*>(&sM[tr][tc0]) = make_float4(t8[0], t8[1], t8[2], t8[3]);
-        *reinterpret_cast<float4*>(&sM[tr][tc0 + 4]) = make_float4(t8[4], t8[5], t8[6], t8[7]);
+        *reinterpret_cast<float4*>(&sA[32 + tr][tc0]) = make_float4(t8[0], t8[1], t8[2], t8[3]);
+        *reinterpret_cast<float4*>(&sA[32 + tr][tc0 + 4]) = make_float4(t8[4], t8[5], t8[6], t8[7]);
       }
       named_bar_sync(bar_sync, kGroup);
       // (3) A10 = -sign A11 T
@@ -847,8 +848,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 8
         for (int m = 0; m < (tr < 16 ? 16 : 32); ++m) {
           const float av = sA[32 + tr][32 + m];
-          const float4 t0 = *reinterpret_cast<const float4*>(&sM[m][tc0]);
-          const float4 t1 = *reinterpret_cast<const float4*>(&sM[m][tc0 + 4]);
+          const float4 t0 = *reinterpret_cast<const float4*>(&sA[32 + m][tc0]);  // T row m
+          const float4 t1 = *reinterpret_cast<const float4*>(&sA[32 + m][tc0 + 4]);
           a8[0] = fmaf(av, t0.x, a8[0]); a8[1] = fmaf(av, t0.y, a8[1]);
           a8[2] = fmaf(av, t0.z, a8[2]); a8[3] = fmaf(av, t0.w, a8[3]);
           a8[4] = fmaf(av, t1.x, a8[4]); a8[5] = fmaf(av, t1.y, a8[5]);
