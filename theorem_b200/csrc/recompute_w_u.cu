@@ -749,16 +749,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int q = 0; q < 16; ++q) x[q] = 0.f;
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
-          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+          float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
 #pragma unroll
           for (int m = 0; m < r; m += 4) {
             const float4 mv = *reinterpret_cast<const float4*>(&sM[base + r][base + m]);
-            s0 = fmaf(mv.x, x[m], s0);
-            s1 = fmaf(mv.y, x[m + 1], s1);
-            s2 = fmaf(mv.z, x[m + 2], s2);
-            s3 = fmaf(mv.w, x[m + 3], s3);
+            s01 = __ffma2_rn(make_float2(mv.x, mv.y), make_float2(x[m], x[m + 1]), s01);
+            s23 = __ffma2_rn(make_float2(mv.z, mv.w), make_float2(x[m + 2], x[m + 3]), s23);
           }
-          x[r] = ((r == j) ? 1.f : 0.f) - sgn * ((s0 + s1) + (s2 + s3));
+          x[r] = ((r == j) ? 1.f : 0.f) - sgn * ((s01.x + s01.y) + (s23.x + s23.y));
         }
         // Only the lower-triangular blocks of sA are ever written; readers
         // below never touch the (unwritten) upper-right blocks.
@@ -770,25 +768,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       //      128 threads = 2 blocks x 16 rows x 4 column groups of 4.
       {
         const int p = mt >> 6, r = (mt >> 2) & 15, c4 = (mt & 3) * 4, base = 32 * p;
-        float t4[4] = {0.f, 0.f, 0.f, 0.f};
+        float2 t01 = make_float2(0.f, 0.f), t23 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int m = 0; m < 16; ++m) {
           const float mv = sM[base + 16 + r][base + m];
           const float4 a = *reinterpret_cast<const float4*>(&sA[base + m][base + c4]);
-          t4[0] = fmaf(mv, a.x, t4[0]); t4[1] = fmaf(mv, a.y, t4[1]);
-          t4[2] = fmaf(mv, a.z, t4[2]); t4[3] = fmaf(mv, a.w, t4[3]);
+          t01 = __ffma2_rn(make_float2(mv, mv), make_float2(a.x, a.y), t01);
+          t23 = __ffma2_rn(make_float2(mv, mv), make_float2(a.z, a.w), t23);
         }
+        const float t4[4] = {t01.x, t01.y, t23.x, t23.y};
         named_bar_sync(bar_sync, kGroup);  // M_00 corners no longer read
         *reinterpret_cast<float4*>(&sM[base + r][base + c4]) = make_float4(t4[0], t4[1], t4[2], t4[3]);
         named_bar_sync(bar_sync, kGroup);
-        float a4[4] = {0.f, 0.f, 0.f, 0.f};
+        float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int m = 0; m < 16; ++m) {
           const float av = sA[base + 16 + r][base + 16 + m];
           const float4 t = *reinterpret_cast<const float4*>(&sM[base + m][base + c4]);
-          a4[0] = fmaf(av, t.x, a4[0]); a4[1] = fmaf(av, t.y, a4[1]);
-          a4[2] = fmaf(av, t.z, a4[2]); a4[3] = fmaf(av, t.w, a4[3]);
+          a01 = __ffma2_rn(make_float2(av, av), make_float2(t.x, t.y), a01);
+          a23 = __ffma2_rn(make_float2(av, av), make_float2(t.z, t.w), a23);
         }
+        const float a4[4] = {a01.x, a01.y, a23.x, a23.y};
         *reinterpret_cast<float4*>(&sA[base + 16 + r][base + c4]) =
             make_float4(-sgn * a4[0], -sgn * a4[1], -sgn * a4[2], -sgn * a4[3]);
       }
@@ -821,40 +821,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       {
-        float t8[8];
+        // packed fp32x2 FMAs (each lane an fmaf, so results are unchanged)
+        float2 t2[4];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) t8[q] = 0.f;
+        for (int q = 0; q < 4; ++q) t2[q] = make_float2(0.f, 0.f);
         // A00 is lower triangular: rows m < 16 only touch columns < 16
 #pragma unroll 8
         for (int m = (tc0 >= 16 ? 16 : 0); m < 32; ++m) {
           const float mv = sM[32 + tr][m];
+          const float2 mm = make_float2(mv, mv);
           const float4 a0 = *reinterpret_cast<const float4*>(&sA[m][tc0]);
           const float4 a1 = *reinterpret_cast<const float4*>(&sA[m][tc0 + 4]);
-          t8[0] = fmaf(mv, a0.x, t8[0]); t8[1] = fmaf(mv, a0.y, t8[1]);
-          t8[2] = fmaf(mv, a0.z, t8[2]); t8[3] = fmaf(mv, a0.w, t8[3]);
-          t8[4] = fmaf(mv, a1.x, t8[4]); t8[5] = fmaf(mv, a1.y, t8[5]);
-          t8[6] = fmaf(mv, a1.z, t8[6]); t8[7] = fmaf(mv, a1.w, t8[7]);
+          t2[0] = __ffma2_rn(mm, make_float2(a0.x, a0.y), t2[0]);
+          t2[1] = __ffma2_rn(mm, make_float2(a0.z, a0.w), t2[1]);
+          t2[2] = __ffma2_rn(mm, make_float2(a1.x, a1.y), t2[2]);
+          t2[3] = __ffma2_rn(mm, make_float2(a1.z, a1.w), t2[3]);
         }
-        *reinterpret_cast<float4*>(&sA[32 + tr][tc0]) = make_float4(t8[0], t8[1], t8[2], t8[3]);
-        *reinterpret_cast<float4*>(&sA[32 + tr][tc0 + 4]) = make_float4(t8[4], t8[5], t8[6], t8[7]);
+        *reinterpret_cast<float4*>(&sA[32 + tr][tc0]) = make_float4(t2[0].x, t2[0].y, t2[1].x, t2[1].y);
+        *reinterpret_cast<float4*>(&sA[32 + tr][tc0 + 4]) = make_float4(t2[2].x, t2[2].y, t2[3].x, t2[3].y);
       }
       named_bar_sync(bar_sync, kGroup);
       // (3) A10 = -sign A11 T
       {
-        float a8[8];
+        float2 a2[4];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) a8[q] = 0.f;
+        for (int q = 0; q < 4; ++q) a2[q] = make_float2(0.f, 0.f);
         // A11 is lower triangular: rows tr < 16 only have columns m < 16
 #pragma unroll 8
         for (int m = 0; m < (tr < 16 ? 16 : 32); ++m) {
           const float av = sA[32 + tr][32 + m];
+          const float2 aa = make_float2(av, av);
           const float4 t0 = *reinterpret_cast<const float4*>(&sA[32 + m][tc0]);  // T row m
           const float4 t1 = *reinterpret_cast<const float4*>(&sA[32 + m][tc0 + 4]);
-          a8[0] = fmaf(av, t0.x, a8[0]); a8[1] = fmaf(av, t0.y, a8[1]);
-          a8[2] = fmaf(av, t0.z, a8[2]); a8[3] = fmaf(av, t0.w, a8[3]);
-          a8[4] = fmaf(av, t1.x, a8[4]); a8[5] = fmaf(av, t1.y, a8[5]);
-          a8[6] = fmaf(av, t1.z, a8[6]); a8[7] = fmaf(av, t1.w, a8[7]);
+          a2[0] = __ffma2_rn(aa, make_float2(t0.x, t0.y), a2[0]);
+          a2[1] = __ffma2_rn(aa, make_float2(t0.z, t0.w), a2[1]);
+          a2[2] = __ffma2_rn(aa, make_float2(t1.x, t1.y), a2[2]);
+          a2[3] = __ffma2_rn(aa, make_float2(t1.z, t1.w), a2[3]);
         }
+        float a8[8] = {a2[0].x, a2[0].y, a2[1].x, a2[1].y, a2[2].x, a2[2].y, a2[3].x, a2[3].y};
         // A10 is final here: straight into the operand tiles (no shared-memory copy)
 #pragma unroll
         for (int q = 0; q < 8; ++q) a8[q] *= -sgn;
