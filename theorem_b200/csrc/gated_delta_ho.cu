@@ -262,10 +262,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint4 p;
           const float* l8 = lv + 8 * q;
           const float* g8 = gv + 8 * q;
-          p.x = pack_bf16x2(fmaf(l8[0], scale, g8[0] * e), fmaf(l8[1], scale, g8[1] * e));
-          p.y = pack_bf16x2(fmaf(l8[2], scale, g8[2] * e), fmaf(l8[3], scale, g8[3] * e));
-          p.z = pack_bf16x2(fmaf(l8[4], scale, g8[4] * e), fmaf(l8[5], scale, g8[5] * e));
-          p.w = pack_bf16x2(fmaf(l8[6], scale, g8[6] * e), fmaf(l8[7], scale, g8[7] * e));
+          // scale L + e G, as packed fp32x2 (each lane an fmaf of the same operands)
+          uint32_t pk[4];
+#pragma unroll
+          for (int z = 0; z < 4; ++z) {
+            const float2 r2 = __ffma2_rn(make_float2(l8[2 * z], l8[2 * z + 1]), make_float2(scale, scale),
+                                         __fmul2_rn(make_float2(g8[2 * z], g8[2 * z + 1]), make_float2(e, e)));
+            pk[z] = pack_bf16x2(r2.x, r2.y);
+          }
+          p = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           *reinterpret_cast<uint4*>(ob + ((uint32_t)((4 * hq + q) ^ (t & 7)) << 4)) = p;
         }
       }
@@ -331,11 +336,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 u2 = bf2_to_f2(uw4[e]);
-              const float n0 = u2.x - xv[8 * q + 2 * e], n1 = u2.y - xv[8 * q + 2 * e + 1];
+              // u - x as fma(x, -1, u): the same rounding as the subtraction
+              const float2 n = __ffma2_rn(make_float2(xv[8 * q + 2 * e], xv[8 * q + 2 * e + 1]),
+                                          make_float2(-1.f, -1.f), u2);
               // v_new (B operand of L) and v_new e^{g_last - g_t} (B operand of U),
               // each rounded to bf16 once from the fp32 difference.
-              vn4[e] = pack_bf16x2(n0, n1);
-              us4[e] = pack_bf16x2(n0 * d, n1 * d);
+              vn4[e] = pack_bf16x2(n.x, n.y);
+              const float2 nd = __fmul2_rn(n, make_float2(d, d));
+              us4[e] = pack_bf16x2(nd.x, nd.y);
             }
             *reinterpret_cast<uint4*>(vrow + off) = make_uint4(vn4[0], vn4[1], vn4[2], vn4[3]);
             *reinterpret_cast<uint4*>(uw + off) = make_uint4(us4[0], us4[1], us4[2], us4[3]);
@@ -382,11 +390,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int s0 = 32 * half + 8 * q + 2 * e;
-              const float f0 = factored ? a_t * sEb[s0] : __expf(g_t - gc[s0]);
-              const float f1 = factored ? a_t * sEb[s0 + 1] : __expf(g_t - gc[s0 + 1]);
-              const float a = (s0 <= t) ? sv[8 * q + 2 * e] * f0 : 0.f;
-              const float bb = (s0 + 1 <= t) ? sv[8 * q + 2 * e + 1] * f1 : 0.f;
-              p4[e] = pack_bf16x2(a, bb);
+              float2 f;
+              if (factored) {
+                f = __fmul2_rn(make_float2(a_t, a_t), make_float2(sEb[s0], sEb[s0 + 1]));
+              } else {
+                f = make_float2(__expf(g_t - gc[s0]), __expf(g_t - gc[s0 + 1]));
+              }
+              const float2 pr = __fmul2_rn(make_float2(sv[8 * q + 2 * e], sv[8 * q + 2 * e + 1]), f);
+              p4[e] = pack_bf16x2((s0 <= t) ? pr.x : 0.f, (s0 + 1 <= t) ? pr.y : 0.f);
             }
             *reinterpret_cast<uint4*>(prow + ((uint32_t)((4 * half + q) ^ (t & 7)) << 4)) =
                 make_uint4(p4[0], p4[1], p4[2], p4[3]);
@@ -414,7 +425,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           float ur[32];
           tmem_ld32(tU + lane_row + qc + 32 * hq, ur);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) S[32 * hq + j] = fmaf(eg, S[32 * hq + j], ur[j]);
+          for (int j = 0; j < 32; j += 2) {
+            const float2 r2 = __ffma2_rn(make_float2(eg, eg), make_float2(S[32 * hq + j], S[32 * hq + j + 1]),
+                                         make_float2(ur[j], ur[j + 1]));
+            S[32 * hq + j] = r2.x;
+            S[32 * hq + j + 1] = r2.y;
+          }
         }
       }
       tc_fence_before();
