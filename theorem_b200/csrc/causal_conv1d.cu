@@ -476,13 +476,28 @@ __global__ void __launch_bounds__(kThreads, 3)
     for (int j = 0; j < RPT + W - 1; ++j) load_row<T>(in + ((RPT * rq + j) * kCh + C * cg) * Ly::ES, xr[j]);
 #pragma unroll
     for (int r = 0; r < RPT; ++r) {
+      // channel pairs as packed fp32x2 (each lane an fmaf / fmul of the same
+      // operands as the scalar form, so the results are unchanged)
       float o[C];
 #pragma unroll
-      for (int j = 0; j < C; ++j) {
-        float acc = bs[j];
+      for (int j = 0; j < C; j += 2) {
+        float2 acc = make_float2(bs[j], bs[j + 1]);
 #pragma unroll
-        for (int k = 0; k < W; ++k) acc = fmaf(xr[r + k][j], wr[j][k], acc);
-        o[j] = SILU ? (sizeof(T) == 2 ? silu_tanh(acc) : silu_f(acc)) : acc;
+        for (int k = 0; k < W; ++k)
+          acc = __ffma2_rn(make_float2(xr[r + k][j], xr[r + k][j + 1]), make_float2(wr[j][k], wr[j + 1][k]), acc);
+        if (SILU && sizeof(T) == 2) {
+          // silu_tanh on the pair: h + h tanh(h), h = x / 2
+          const float2 h = __fmul2_rn(make_float2(0.5f, 0.5f), acc);
+          float t0, t1;
+          asm("tanh.approx.f32 %0, %1;" : "=f"(t0) : "f"(h.x));
+          asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(h.y));
+          const float2 sv = __ffma2_rn(h, make_float2(t0, t1), h);
+          o[j] = sv.x;
+          o[j + 1] = sv.y;
+        } else {
+          o[j] = SILU ? silu_f(acc.x) : acc.x;
+          o[j + 1] = SILU ? silu_f(acc.y) : acc.y;
+        }
       }
       if (GL > 0) {
         float ss = 0.f;
@@ -492,7 +507,11 @@ __global__ void __launch_bounds__(kThreads, 3)
         for (int m = 1; m < GL; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
         const float rn = rsqrtf(ss + 1e-6f);
 #pragma unroll
-        for (int j = 0; j < C; ++j) o[j] *= rn;
+        for (int j = 0; j < C; j += 2) {
+          const float2 sc2 = __fmul2_rn(make_float2(o[j], o[j + 1]), make_float2(rn, rn));
+          o[j] = sc2.x;
+          o[j + 1] = sc2.y;
+        }
       }
       store_row<T>(out + ((RPT * rq + r) * kCh + C * cg) * Ly::ES, o);
     }
