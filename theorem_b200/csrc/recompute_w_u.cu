@@ -674,11 +674,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto put_a8 = [&](const float* a, int t, int c0, const float* sc, int hh, int row0) {
       const float* fk = sc + 128 + c0;
       const float* fb = sc + c0;
-      uint4 pw, pu;
-      pw.x = pack_bf16x2(a[0] * fk[0], a[1] * fk[1]); pw.y = pack_bf16x2(a[2] * fk[2], a[3] * fk[3]);
-      pw.z = pack_bf16x2(a[4] * fk[4], a[5] * fk[5]); pw.w = pack_bf16x2(a[6] * fk[6], a[7] * fk[7]);
-      pu.x = pack_bf16x2(a[0] * fb[0], a[1] * fb[1]); pu.y = pack_bf16x2(a[2] * fb[2], a[3] * fb[3]);
-      pu.z = pack_bf16x2(a[4] * fb[4], a[5] * fb[5]); pu.w = pack_bf16x2(a[6] * fb[6], a[7] * fb[7]);
+      uint32_t w4[4], u4[4];
+#pragma unroll
+      for (int z = 0; z < 4; ++z) {  // packed fp32x2 products (same rounding as scalar)
+        const float2 a2 = make_float2(a[2 * z], a[2 * z + 1]);
+        const float2 pw2 = __fmul2_rn(a2, make_float2(fk[2 * z], fk[2 * z + 1]));
+        const float2 pu2 = __fmul2_rn(a2, make_float2(fb[2 * z], fb[2 * z + 1]));
+        w4[z] = pack_bf16x2(pw2.x, pw2.y);
+        u4[z] = pack_bf16x2(pu2.x, pu2.y);
+      }
+      const uint4 pw = make_uint4(w4[0], w4[1], w4[2], w4[3]), pu = make_uint4(u4[0], u4[1], u4[2], u4[3]);
       *reinterpret_cast<uint4*>(gb + Ly::G_AW + sw128_offset(t, c0, 64, 2)) = pw;
       *reinterpret_cast<uint4*>(gb + Ly::G_AU + sw128_offset(t, c0, 64, 2)) = pu;
       if (a_out != nullptr) {
@@ -715,11 +720,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j > 2 * sp + 1) break;  // warp-uniform
           const int cc = 8 * j + 2 * (lane & 3);
           if (factored) {
-            const float fb0 = sc[256 + cc], fb1 = sc[256 + cc + 1];
-            m0[j].x = (cc < r0) ? fa0 * kv[4 * j] * fb0 : 0.f;
-            m0[j].y = (cc + 1 < r0) ? fa0 * kv[4 * j + 1] * fb1 : 0.f;
-            m1[j].x = (cc < r1) ? fa1 * kv[4 * j + 2] * fb0 : 0.f;
-            m1[j].y = (cc + 1 < r1) ? fa1 * kv[4 * j + 3] * fb1 : 0.f;
+            const float2 fb = make_float2(sc[256 + cc], sc[256 + cc + 1]);
+            // (fa kv) fb, left to right as the scalar form, as packed fp32x2
+            const float2 p0 = __fmul2_rn(__fmul2_rn(make_float2(fa0, fa0), make_float2(kv[4 * j], kv[4 * j + 1])), fb);
+            const float2 p1 =
+                __fmul2_rn(__fmul2_rn(make_float2(fa1, fa1), make_float2(kv[4 * j + 2], kv[4 * j + 3])), fb);
+            m0[j].x = (cc < r0) ? p0.x : 0.f;
+            m0[j].y = (cc + 1 < r0) ? p0.y : 0.f;
+            m1[j].x = (cc < r1) ? p1.x : 0.f;
+            m1[j].y = (cc + 1 < r1) ? p1.y : 0.f;
           } else {
             const float gc0 = sc[64 + cc], gc1 = sc[64 + cc + 1];
             m0[j].x = (cc < r0) ? b0 * kv[4 * j] * __expf(g0 - gc0) : 0.f;
