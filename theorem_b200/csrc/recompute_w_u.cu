@@ -692,6 +692,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<float4*>(dst + 4) = make_float4(a[4], a[5], a[6], a[7]);
       }
     };
+    // The same for 4 consecutive entries (columns c0..c0+3, c0 % 4 == 0).
+    auto put_a4 = [&](const float* a, int t, int c0, const float* sc, int hh, int row0) {
+      const float* fk = sc + 128 + c0;
+      const float* fb = sc + c0;
+      const float2 a01 = make_float2(a[0], a[1]), a23 = make_float2(a[2], a[3]);
+      const float2 w01 = __fmul2_rn(a01, make_float2(fk[0], fk[1])), w23 = __fmul2_rn(a23, make_float2(fk[2], fk[3]));
+      const float2 u01 = __fmul2_rn(a01, make_float2(fb[0], fb[1])), u23 = __fmul2_rn(a23, make_float2(fb[2], fb[3]));
+      const uint32_t off = sw128_offset(t, c0, 64, 2);
+      *reinterpret_cast<uint2*>(gb + Ly::G_AW + off) = make_uint2(pack_bf16x2(w01.x, w01.y), pack_bf16x2(w23.x, w23.y));
+      *reinterpret_cast<uint2*>(gb + Ly::G_AU + off) = make_uint2(pack_bf16x2(u01.x, u01.y), pack_bf16x2(u23.x, u23.y));
+      if (a_out != nullptr)
+        *reinterpret_cast<float4*>(a_out + ((long long)(row0 + t) * H + hh) * 64 + c0) = make_float4(a[0], a[1], a[2], a[3]);
+    };
     for (int i = grp; i < n_local; i += 2) {
       const int u = blockIdx.x + i * gridDim.x;
       const int st = i % kStages;
@@ -809,7 +822,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       //     it: no barrier between the products and the write). Alongside: the diagonal
       //     32-blocks A00, A11 are final, so their operand entries are written now
       //     (thread: block mt/64, row (mt/2)%32, 16 columns).
-      const int tr = mt >> 2, tc0 = (mt & 3) * 8;
+      // products: thread = rows 2 rp, 2 rp + 1 x columns tc .. tc + 3 (register-blocked:
+      // one float4 of each M / A row serves four m)
+      const int rp = mt >> 3, tc = (mt & 7) * 4;
       {
         const int blk = mt >> 6, rr = (mt >> 1) & 31, cb0 = (mt & 1) * 16;
         const int t = 32 * blk + rr;
@@ -830,48 +845,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       {
-        // packed fp32x2 FMAs (each lane an fmaf, so results are unchanged)
-        float2 t2[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) t2[q] = make_float2(0.f, 0.f);
+        // packed fp32x2 FMAs (each lane an fmaf, summed over m in order as before)
+        float2 t0a = make_float2(0.f, 0.f), t0b = t0a, t1a = t0a, t1b = t0a;
         // A00 is lower triangular: rows m < 16 only touch columns < 16
-#pragma unroll 8
-        for (int m = (tc0 >= 16 ? 16 : 0); m < 32; ++m) {
-          const float mv = sM[32 + tr][m];
-          const float2 mm = make_float2(mv, mv);
-          const float4 a0 = *reinterpret_cast<const float4*>(&sA[m][tc0]);
-          const float4 a1 = *reinterpret_cast<const float4*>(&sA[m][tc0 + 4]);
-          t2[0] = __ffma2_rn(mm, make_float2(a0.x, a0.y), t2[0]);
-          t2[1] = __ffma2_rn(mm, make_float2(a0.z, a0.w), t2[1]);
-          t2[2] = __ffma2_rn(mm, make_float2(a1.x, a1.y), t2[2]);
-          t2[3] = __ffma2_rn(mm, make_float2(a1.z, a1.w), t2[3]);
+#pragma unroll 2
+        for (int m4 = (tc >= 16 ? 16 : 0); m4 < 32; m4 += 4) {
+          const float4 ma = *reinterpret_cast<const float4*>(&sM[32 + 2 * rp][m4]);
+          const float4 mb = *reinterpret_cast<const float4*>(&sM[33 + 2 * rp][m4]);
+          const float mav[4] = {ma.x, ma.y, ma.z, ma.w}, mbv[4] = {mb.x, mb.y, mb.z, mb.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float4 a = *reinterpret_cast<const float4*>(&sA[m4 + e][tc]);
+            const float2 alo = make_float2(a.x, a.y), ahi = make_float2(a.z, a.w);
+            t0a = __ffma2_rn(make_float2(mav[e], mav[e]), alo, t0a);
+            t0b = __ffma2_rn(make_float2(mav[e], mav[e]), ahi, t0b);
+            t1a = __ffma2_rn(make_float2(mbv[e], mbv[e]), alo, t1a);
+            t1b = __ffma2_rn(make_float2(mbv[e], mbv[e]), ahi, t1b);
+          }
         }
-        *reinterpret_cast<float4*>(&sA[32 + tr][tc0]) = make_float4(t2[0].x, t2[0].y, t2[1].x, t2[1].y);
-        *reinterpret_cast<float4*>(&sA[32 + tr][tc0 + 4]) = make_float4(t2[2].x, t2[2].y, t2[3].x, t2[3].y);
+        *reinterpret_cast<float4*>(&sA[32 + 2 * rp][tc]) = make_float4(t0a.x, t0a.y, t0b.x, t0b.y);
+        *reinterpret_cast<float4*>(&sA[33 + 2 * rp][tc]) = make_float4(t1a.x, t1a.y, t1b.x, t1b.y);
       }
       named_bar_sync(bar_sync, kGroup);
       // (3) A10 = -sign A11 T
       {
-        float2 a2[4];
+        float2 a0a = make_float2(0.f, 0.f), a0b = a0a, a1a = a0a, a1b = a0a;
+        // A11 is lower triangular: rows 2 rp, 2 rp + 1 < 16 only have columns m < 16
+#pragma unroll 2
+        for (int m4 = 0; m4 < (rp < 8 ? 16 : 32); m4 += 4) {
+          const float4 xa = *reinterpret_cast<const float4*>(&sA[32 + 2 * rp][32 + m4]);
+          const float4 xb = *reinterpret_cast<const float4*>(&sA[33 + 2 * rp][32 + m4]);
+          const float xav[4] = {xa.x, xa.y, xa.z, xa.w}, xbv[4] = {xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) a2[q] = make_float2(0.f, 0.f);
-        // A11 is lower triangular: rows tr < 16 only have columns m < 16
-#pragma unroll 8
-        for (int m = 0; m < (tr < 16 ? 16 : 32); ++m) {
-          const float av = sA[32 + tr][32 + m];
-          const float2 aa = make_float2(av, av);
-          const float4 t0 = *reinterpret_cast<const float4*>(&sA[32 + m][tc0]);  // T row m
-          const float4 t1 = *reinterpret_cast<const float4*>(&sA[32 + m][tc0 + 4]);
-          a2[0] = __ffma2_rn(aa, make_float2(t0.x, t0.y), a2[0]);
-          a2[1] = __ffma2_rn(aa, make_float2(t0.z, t0.w), a2[1]);
-          a2[2] = __ffma2_rn(aa, make_float2(t1.x, t1.y), a2[2]);
-          a2[3] = __ffma2_rn(aa, make_float2(t1.z, t1.w), a2[3]);
+          for (int e = 0; e < 4; ++e) {
+            const float4 tt = *reinterpret_cast<const float4*>(&sA[32 + m4 + e][tc]);  // T row m
+            const float2 tlo = make_float2(tt.x, tt.y), thi = make_float2(tt.z, tt.w);
+            a0a = __ffma2_rn(make_float2(xav[e], xav[e]), tlo, a0a);
+            a0b = __ffma2_rn(make_float2(xav[e], xav[e]), thi, a0b);
+            a1a = __ffma2_rn(make_float2(xbv[e], xbv[e]), tlo, a1a);
+            a1b = __ffma2_rn(make_float2(xbv[e], xbv[e]), thi, a1b);
+          }
         }
-        float a8[8] = {a2[0].x, a2[0].y, a2[1].x, a2[1].y, a2[2].x, a2[2].y, a2[3].x, a2[3].y};
         // A10 is final here: straight into the operand tiles (no shared-memory copy)
-#pragma unroll
-        for (int q = 0; q < 8; ++q) a8[q] *= -sgn;
-        put_a8(a8, 32 + tr, tc0, sc, hh, row0);
+        const float r0[4] = {-sgn * a0a.x, -sgn * a0a.y, -sgn * a0b.x, -sgn * a0b.y};
+        const float r1[4] = {-sgn * a1a.x, -sgn * a1a.y, -sgn * a1b.x, -sgn * a1b.y};
+        put_a4(r0, 32 + 2 * rp, tc, sc, hh, row0);
+        put_a4(r1, 33 + 2 * rp, tc, sc, hh, row0);
       }
       fence_proxy_async_smem();
       mbar_arrive(&afull[grp]);
