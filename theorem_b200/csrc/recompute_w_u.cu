@@ -446,14 +446,14 @@ __device__ __forceinline__ void wu_epilogue(uint8_t* gb, uint32_t tbase, int grp
     const int ncol = is_w ? K : V;
     constexpr int NMAX = K > V ? K : V;
 #pragma unroll
-    for (int c0 = 0; c0 < NMAX; c0 += 32) {
-      float v[32];
-      tmem_ld32(tW + c0, v);
+    for (int c0 = 0; c0 < NMAX; c0 += 64) {
+      float v[64];
+      tmem_ld64(tW + c0, v);
       if (c0 < ncol) {
         uint8_t* box = dst + (c0 / 64) * 8192 + r * 128;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t ck = (uint32_t)(((c0 % 64) / 8 + q) ^ (r & 7));
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t ck = (uint32_t)(q ^ (r & 7));
           *reinterpret_cast<uint4*>(box + (ck << 4)) =
               make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
                          pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
