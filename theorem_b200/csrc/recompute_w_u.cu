@@ -561,6 +561,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < K / 64; ++j) tma_load_3d(stg + j * 8192, &tm_k, &full[st], j * 64, hh, row0);
 #pragma unroll
         for (int j = 0; j < V / 64; ++j) tma_load_3d(stg + Ly::KB + j * 8192, &tm_v, &full[st], j * 64, hh, row0);
+        if (i + 1 < n_local) {
+          // the next unit's tiles into L2 now: its load is issued once a stage frees
+          // (a unit later) and then comes from L2 instead of HBM
+          const int un = u + gridDim.x;
+          const int hn = un % H, bn = un / H;
+          const int rn = (bn / NT) * T_len + (bn % NT) * 64;
+#pragma unroll
+          for (int j = 0; j < K / 64; ++j) tma_prefetch_l2_3d(&tm_k, j * 64, hn, rn);
+#pragma unroll
+          for (int j = 0; j < V / 64; ++j) tma_prefetch_l2_3d(&tm_v, j * 64, hn, rn);
+        }
       }
       // Decay e^{g_r - g_c} = e^{g_r - g_m} e^{g_m - g_c} about the middle g_m of the
       // chunk's gate range (each factor at most e^{range/2}; ranges over 120 keep one
