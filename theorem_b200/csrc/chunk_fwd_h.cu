@@ -254,20 +254,20 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint4* p = reinterpret_cast<uint4*>(stage + Ly::K_BYTES + sw128_offset(t, j, kBT, 2));
               uint4 r = *p;
               const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&r);
+              uint32_t o4[4], s4[4];
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                float2 f = __bfloat1622float2(h2[q]);
-                un[2 * q] = f.x - xr[j + 2 * q];
-                un[2 * q + 1] = f.y - xr[j + 2 * q + 1];
+                // u - x as fma(x, -1, u) and the decayed copy, packed fp32x2 (same roundings)
+                const float2 f = __bfloat1622float2(h2[q]);
+                const float2 d2 = __ffma2_rn(make_float2(xr[j + 2 * q], xr[j + 2 * q + 1]), make_float2(-1.f, -1.f), f);
+                const float2 e2 = __fmul2_rn(d2, make_float2(dec, dec));
+                un[2 * q] = d2.x;
+                un[2 * q + 1] = d2.y;
+                o4[q] = pack_bf16x2(d2.x, d2.y);
+                s4[q] = pack_bf16x2(e2.x, e2.y);
               }
-              uint4 o;
-              o.x = pack_bf16x2(un[0], un[1]); o.y = pack_bf16x2(un[2], un[3]);
-              o.z = pack_bf16x2(un[4], un[5]); o.w = pack_bf16x2(un[6], un[7]);
-              *reinterpret_cast<uint4*>(vn + sw128_offset(t, j, kBT, 2)) = o;
-              uint4 sc;
-              sc.x = pack_bf16x2(un[0] * dec, un[1] * dec); sc.y = pack_bf16x2(un[2] * dec, un[3] * dec);
-              sc.z = pack_bf16x2(un[4] * dec, un[5] * dec); sc.w = pack_bf16x2(un[6] * dec, un[7] * dec);
-              *p = sc;
+              *reinterpret_cast<uint4*>(vn + sw128_offset(t, j, kBT, 2)) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+              *p = make_uint4(s4[0], s4[1], s4[2], s4[3]);
             } else {
 #pragma unroll
               for (int q = 0; q < 8; q += 4) {
@@ -337,7 +337,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float eg = __expf(gl);
       if (srow_ok) {
 #pragma unroll
-        for (int j = 0; j < kVT; ++j) S[j] = fmaf(eg, S[j], ur[j]);
+        for (int j = 0; j < kVT; j += 2) {
+          const float2 r2 = __ffma2_rn(make_float2(eg, eg), make_float2(S[j], S[j + 1]), make_float2(ur[j], ur[j + 1]));
+          S[j] = r2.x;
+          S[j + 1] = r2.y;
+        }
       }
     }
     tc_fence_before();
