@@ -163,6 +163,22 @@ int thm_gated_delta_fwd_ho(const void* q, const void* k, const void* w, const vo
                            int V, int dtype, thm_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * thm_sp_prefix_fold -- states entering consecutive segments of a sequence
+ * split along T (sequence parallel). The delta-rule recurrence of a segment
+ * (kernels/chunk_fwd_h/kernel.py:61-138 with the delta rule) maps its entering
+ * state affinely, h_out = M h_in + S; for R segments in order:
+ *
+ *   out[0] = x0 (or 0 when x0 is NULL),  out[r+1] = M[r] out[r] + S[r]
+ *
+ * for r < nout - 1. M [nout-1, BH, K, K], S [nout-1, BH, K, V], x0 [BH, K, V],
+ * out [nout, BH, K, V], all fp32. K <= 128, K % 4 == 0, V % 32 == 0. No
+ * reference counterpart as one call (the reference has no sequence-parallel
+ * path); it replaces a loop of small batched matrix products.
+ * ------------------------------------------------------------------------- */
+int thm_sp_prefix_fold(const float* M, const float* S, const float* x0, float* out, int nout, int BH, int K, int V,
+                       thm_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Utilities
  * ------------------------------------------------------------------------- */
 /* Human-readable name of a thm_status. */

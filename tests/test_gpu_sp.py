@@ -85,3 +85,32 @@ def test_delta_h_without_state_output():
                                       want_h=False)
     assert none is None
     assert torch.equal(vn, vn2) and torch.equal(fin, fin2)
+
+
+@pytest.mark.parametrize("R,BH,K,V,with_x0,nout", [(7, 16, 128, 128, False, None), (3, 5, 64, 96, True, None),
+                                                  (4, 2, 128, 256, True, 3), (1, 3, 32, 32, False, 1)])
+def test_prefix_fold_kernel_matches_float64(R, BH, K, V, with_x0, nout):
+    """One-launch fold x_{r+1} = M_r x_r + S_r against the same recurrence in float64."""
+    from theorem_b200 import ops
+    gen = torch.Generator().manual_seed(R * 100 + K)
+    Ms = torch.randn(R, BH, K, K, generator=gen) / K ** 0.5
+    Ss = torch.randn(R, BH, K, V, generator=gen)
+    x0 = torch.randn(BH, K, V, generator=gen) if with_x0 else None
+    out = ops.sp_prefix_fold(Ms.cuda(), Ss.cuda(), None if x0 is None else x0.cuda(), nout=nout).cpu().double()
+    n = R + 1 if nout is None else nout
+    x = torch.zeros(BH, K, V, dtype=torch.float64) if x0 is None else x0.double()
+    ref = [x]
+    for r in range(n - 1):
+        x = torch.matmul(Ms[r].double(), x) + Ss[r].double()
+        ref.append(x)
+    ref = torch.stack(ref)
+    assert out.shape == ref.shape
+    assert torch.allclose(out, ref, rtol=1e-4, atol=1e-4), float((out - ref).abs().max())
+
+
+def test_prefix_fold_rejects_unsupported():
+    from theorem_b200 import ops
+    with pytest.raises(AssertionError):  # K > 128
+        ops.sp_prefix_fold(torch.zeros(2, 1, 256, 256).cuda(), torch.zeros(2, 1, 256, 32).cuda())
+    with pytest.raises(AssertionError):  # V % 32 != 0
+        ops.sp_prefix_fold(torch.zeros(2, 1, 64, 64).cuda(), torch.zeros(2, 1, 64, 48).cuda())

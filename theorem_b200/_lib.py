@@ -37,6 +37,7 @@ _SIGNATURES = {
     "thm_build_A_fwd": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
     "thm_chunk_local_cumsum_fwd": [_P, _P, _I, _I, _I, _F, _P],
     "thm_gated_delta_fwd_ho": [_P, _P, _P, _P, _P, _P, _P, _P, _F, _I, _I, _I, _I, _I, _I, _P],
+    "thm_sp_prefix_fold": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
     "thm_status_string": [_I],
     "thm_get_device_status": [ctypes.POINTER(_I), _I],
     "thm_version": [],

@@ -181,6 +181,29 @@ def gated_delta_fwd_ho(q, k, w, u, g, scale: float, h0=None, want_final: bool = 
     return o, final
 
 
+def sp_prefix_fold(Ms, Ss, x0=None, nout: int | None = None, out=None):
+    """States entering consecutive segments: out[0] = x0 (or 0), out[r+1] =
+    Ms[r] out[r] + Ss[r]. Ms [R, BH, K, K], Ss [R, BH, K, V], x0 [BH, K, V] fp32;
+    returns out [nout, BH, K, V] (nout <= R + 1, default R + 1). One launch; the
+    state of each (bh, 32-column tile) stays in shared memory across the steps."""
+    _cuda(Ms, Ss, x0)
+    _contig(Ms, Ss, x0)
+    R, BH, K, V = Ss.shape
+    assert Ms.shape == (R, BH, K, K), f"Ms shape {tuple(Ms.shape)} != {(R, BH, K, K)}"
+    assert Ms.dtype == torch.float32 and Ss.dtype == torch.float32, "segment maps must be float32"
+    if x0 is not None:
+        assert x0.shape == (BH, K, V) and x0.dtype == torch.float32
+    nout = R + 1 if nout is None else int(nout)
+    assert 1 <= nout <= R + 1
+    if out is None:
+        out = torch.empty(nout, BH, K, V, device=Ss.device, dtype=torch.float32)
+    assert out.shape == (nout, BH, K, V) and out.dtype == torch.float32 and out.is_contiguous()
+    st = L.stream_of(Ss)
+    L.check(L.load().thm_sp_prefix_fold(L.ptr(Ms), L.ptr(Ss), L.ptr(x0), L.ptr(out), nout, BH, K, V, st),
+            "thm_sp_prefix_fold")
+    return out
+
+
 def build_A(k, beta, g, sign: int = -1, out=None):
     """Per-chunk WY matrix A = (I + sign*M)^-1, M = strict_tril(beta_i k_i.k_j e^{g_i-g_j})
     (kernels/recompute_w_u/reference.py:48-91 ``_build_A`` is sign = -1). Returns

@@ -19,7 +19,7 @@ segment is one more "sequence" of the batch ([B, T, H, X] viewed as
   1. (M_r, S_r) of every segment: two chunk_fwd_h launches, no per-chunk states
      written;
   2. the prefix fold over segments: R-1 small K x K by K x V products per head in
-     fp32 (plain ``torch.matmul``);
+     fp32, one launch of ``ops.sp_prefix_fold`` on the GPU;
   3. state recurrence + output of every segment from its entering state
      (the fused gated_delta_fwd_ho kernel for bf16, K = V = 128).
 
@@ -37,11 +37,25 @@ import torch.distributed as dist
 from . import ops
 
 
+_CONST: dict = {}
+
+
+def _constants(k):
+    """The zero u and identity h0 of the M summary for k's shape, kept across calls
+    (read-only inputs of the kernel, so one copy per shape and device serves all)."""
+    B, T, H, K = k.shape
+    key = (tuple(k.shape), k.dtype, k.device)
+    if key not in _CONST:
+        if len(_CONST) > 8:
+            _CONST.clear()
+        _CONST[key] = (torch.zeros_like(k),
+                       torch.eye(K, device=k.device, dtype=torch.float32).expand(B, H, K, K).contiguous())
+    return _CONST[key]
+
+
 def segment_summary(k, w, u, g):
     """(M, S) of each sequence of the batch: M [B,H,K,K], S [B,H,K,V] fp32."""
-    B, T, H, K = k.shape
-    zero_u = torch.zeros_like(k)
-    eye = torch.eye(K, device=k.device, dtype=torch.float32).expand(B, H, K, K).contiguous()
+    zero_u, eye = _constants(k)
     _, _, M = ops.chunk_fwd_h(k, zero_u, g, w=w, h0=eye, mode=1, want_final=True, want_h=False)
     _, _, S = ops.chunk_fwd_h(k, u, g, w=w, h0=None, mode=1, want_final=True, want_h=False)
     return M, S
@@ -51,11 +65,21 @@ def _acc_dtype(t):
     return torch.float64 if t.dtype == torch.float64 else torch.float32
 
 
+def _fold_on_gpu(Ss):
+    return Ss.is_cuda and Ss.dtype != torch.float64
+
+
 def prefix_states(Ms, Ss, h0=None):
     """States entering each of R consecutive segments, [R,B,H,K,V], from the
     segment summaries Ms [R,B,H,K,K], Ss [R,B,H,K,V] and the state h0 entering
-    the first (None = 0)."""
+    the first (None = 0). On the GPU one ``ops.sp_prefix_fold`` launch; CPU
+    tensors (the gloo tests of the multi-rank logic) use torch products."""
     R, B, H, K, V = Ss.shape
+    if _fold_on_gpu(Ss):
+        x0 = None if h0 is None else h0.float().reshape(B * H, K, V).contiguous()
+        out = ops.sp_prefix_fold(Ms.float().reshape(R, B * H, K, K).contiguous(),
+                                 Ss.float().reshape(R, B * H, K, V).contiguous(), x0, nout=R)
+        return out.reshape(R, B, H, K, V)
     dt = _acc_dtype(Ss)
     out = torch.empty(R, B * H, K, V, dtype=dt, device=Ss.device)
     if h0 is None:
@@ -72,6 +96,13 @@ def prefix_states(Ms, Ss, h0=None):
 def prefix_state(Ms, Ss, upto: int, h0=None):
     """State entering segment ``upto`` (``upto`` = R: the state after the last one)."""
     R, B, H, K, V = Ss.shape
+    if _fold_on_gpu(Ss):
+        x0 = None if h0 is None else h0.float().reshape(B * H, K, V).contiguous()
+        if upto == 0:
+            return torch.zeros(B, H, K, V, device=Ss.device) if x0 is None else x0.reshape(B, H, K, V).clone()
+        out = ops.sp_prefix_fold(Ms[:upto].float().reshape(upto, B * H, K, K).contiguous(),
+                                 Ss[:upto].float().reshape(upto, B * H, K, V).contiguous(), x0)
+        return out[upto].reshape(B, H, K, V)
     dt = _acc_dtype(Ss)
     h = torch.zeros(B, H, K, V, dtype=dt, device=Ss.device) if h0 is None else h0.to(dt).clone()
     for r in range(upto):
@@ -80,7 +111,17 @@ def prefix_state(Ms, Ss, upto: int, h0=None):
 
 
 def compose(Ms, Ss):
-    """(M, S) of R consecutive segments taken as one."""
+    """(M, S) of R consecutive segments taken as one. On the GPU one fold over
+    K + V columns: x_0 = [I | 0], x_{r+1} = M_r x_r + [0 | S_r] ends at
+    [prod M | composed S]."""
+    if _fold_on_gpu(Ss) and Ss.shape[0] > 1:
+        R, B, H, K, V = Ss.shape
+        BH = B * H
+        eye = torch.eye(K, device=Ss.device, dtype=torch.float32).expand(BH, K, K)
+        x0 = torch.cat([eye, torch.zeros(BH, K, V, device=Ss.device)], dim=-1).contiguous()
+        Sx = torch.cat([torch.zeros(R, BH, K, K, device=Ss.device), Ss.float().reshape(R, BH, K, V)], dim=-1)
+        out = ops.sp_prefix_fold(Ms.float().reshape(R, BH, K, K).contiguous(), Sx.contiguous(), x0)[R]
+        return out[..., :K].reshape(B, H, K, K), out[..., K:].reshape(B, H, K, V)
     dt = _acc_dtype(Ss)
     M, S = Ms[0].to(dt), Ss[0].to(dt)
     for r in range(1, Ss.shape[0]):
