@@ -192,6 +192,17 @@ int thm_get_device_status(int* device_status, int reset);
 /* ABI version: (major << 16) | minor. */
 int thm_version(void);
 
+/* Test hook for the timeout path: launches one warp that waits, through the
+ * same bounded mbarrier wait every kernel here uses, on a barrier nobody
+ * arrives on, for limit_ns nanoseconds (1e3 .. 1e8). The wait runs out, the
+ * kernel records THM_ERR_TIMEOUT in the device status word and returns (no
+ * TMA or tensor-core work is in flight), so thm_get_device_status() then
+ * reports THM_ERR_TIMEOUT until reset; if waited_out (device int) is not NULL
+ * it receives 1 when the wait ran out, 0 otherwise. No reference counterpart as
+ * a call: it stands in for the reference harness's per-cell failure recording
+ * (benchmarks/pytorch_baseline.py:99-110), which a test can trigger on demand. */
+int thm_selftest_wait_timeout(long long limit_ns, int* waited_out, thm_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,7 +11,7 @@ from tests.synth import deltanet_inputs
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-TOL = 2e-2  # bf16 activations, state rounded to bf16 as an MMA operand
+TOL = 1e-2  # the north star's bf16 tolerance (kernels/chunk_fwd_o/task.yml rtol = atol = 1e-2)
 
 
 def _inputs(B, T, H, seed, K=128, V=128):

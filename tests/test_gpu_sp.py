@@ -11,7 +11,7 @@ from tests.synth import deltanet_inputs
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-TOL = 2e-2
+TOL = 1e-2  # the north star's bf16 tolerance (rtol = atol = 1e-2)
 
 
 def _inputs(B, T, H, K, V, seed, dtype=torch.bfloat16):
@@ -114,3 +114,43 @@ def test_prefix_fold_rejects_unsupported():
         ops.sp_prefix_fold(torch.zeros(2, 1, 256, 256).cuda(), torch.zeros(2, 1, 256, 32).cuda())
     with pytest.raises(AssertionError):  # V % 32 != 0
         ops.sp_prefix_fold(torch.zeros(2, 1, 64, 64).cuda(), torch.zeros(2, 1, 64, 48).cuda())
+
+
+def _maps(R, B, H, K, V, seed):
+    gen = torch.Generator().manual_seed(seed)
+    Ms = torch.randn(R, B, H, K, K, generator=gen) / K ** 0.5
+    Ss = torch.randn(R, B, H, K, V, generator=gen)
+    h0 = torch.randn(B, H, K, V, generator=gen)
+    return Ms, Ss, h0
+
+
+@pytest.mark.parametrize("K,V", [(128, 128), (64, 128)])
+def test_compose_gpu_fold_matches_float64_branch(K, V):
+    """compose() on the GPU (one fold over K + V columns from [I | 0]) against its
+    float64 CPU branch (the same products in a Python loop)."""
+    from theorem_b200 import sp
+    Ms, Ss, _ = _maps(5, 2, 3, K, V, seed=K + V)
+    M_gpu, S_gpu = sp.compose(Ms.cuda(), Ss.cuda())
+    M_ref, S_ref = sp.compose(Ms.double(), Ss.double())
+    assert M_gpu.shape == (2, 3, K, K) and S_gpu.shape == (2, 3, K, V)
+    assert torch.allclose(M_gpu.cpu().double(), M_ref, rtol=1e-4, atol=1e-4), float((M_gpu.cpu() - M_ref).abs().max())
+    assert torch.allclose(S_gpu.cpu().double(), S_ref, rtol=1e-4, atol=1e-4), float((S_gpu.cpu() - S_ref).abs().max())
+
+
+@pytest.mark.parametrize("K,V", [(128, 128), (64, 128)])
+@pytest.mark.parametrize("with_h0", [True, False])
+def test_prefix_state_gpu_matches_float64_branch(K, V, with_h0):
+    """prefix_state(upto) on the GPU (the fold over Ms[:upto]) against the float64
+    CPU branch, for upto = 0 (the entering state itself), 1 and R (after the last)."""
+    from theorem_b200 import sp
+    R = 4
+    Ms, Ss, h0 = _maps(R, 1, 2, K, V, seed=3 * K + V)
+    h0 = h0 if with_h0 else None
+    for upto in (0, 1, R):
+        got = sp.prefix_state(Ms.cuda(), Ss.cuda(), upto, None if h0 is None else h0.cuda())
+        ref = sp.prefix_state(Ms.double(), Ss.double(), upto, None if h0 is None else h0.double())
+        assert got.shape == (1, 2, K, V)
+        assert torch.allclose(got.cpu().double(), ref, rtol=1e-4, atol=1e-4), (upto, float((got.cpu() - ref).abs().max()))
+    starts = sp.prefix_states(Ms.cuda(), Ss.cuda(), None if h0 is None else h0.cuda())
+    ref = sp.prefix_states(Ms.double(), Ss.double(), None if h0 is None else h0.double())
+    assert torch.allclose(starts.cpu().double(), ref, rtol=1e-4, atol=1e-4)

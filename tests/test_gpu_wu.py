@@ -127,5 +127,5 @@ def test_fused_A_steep_gates(sign):
     w, u = ops.recompute_w_u(k.to(DEV), v.to(DEV), beta.to(DEV), None, g.to(DEV), a_mode=sign)
     A = orc.build_A(k.float(), beta, g, sign)
     rw, ru = orc.recompute_w_u(k.float(), v.float(), beta, A, g)
-    assert_close(w.float().cpu().double(), torch.from_numpy(rw), 2e-2, 2e-2, "w")
-    assert_close(u.float().cpu().double(), torch.from_numpy(ru), 2e-2, 2e-2, "u")
+    assert_close(w.float().cpu().double(), torch.from_numpy(rw), TOL, TOL, "w")
+    assert_close(u.float().cpu().double(), torch.from_numpy(ru), TOL, TOL, "u")

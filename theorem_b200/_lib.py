@@ -38,6 +38,7 @@ _SIGNATURES = {
     "thm_chunk_local_cumsum_fwd": [_P, _P, _I, _I, _I, _F, _P],
     "thm_gated_delta_fwd_ho": [_P, _P, _P, _P, _P, _P, _P, _P, _F, _I, _I, _I, _I, _I, _I, _P],
     "thm_sp_prefix_fold": [_P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "thm_selftest_wait_timeout": [ctypes.c_longlong, _P, _P],
     "thm_status_string": [_I],
     "thm_get_device_status": [ctypes.POINTER(_I), _I],
     "thm_version": [],

@@ -81,7 +81,8 @@ int thm_get_device_status(int* device_status, int reset) {
   if (cudaDeviceSynchronize() != cudaSuccess) return THM_ERR_CUDA;
   unsigned acc = 0, s = 0;
   int (*readers[])(unsigned*, int) = {thm_internal_status_conv, thm_internal_status_wu, thm_internal_status_h,
-                                      thm_internal_status_o, thm_internal_status_ho};
+                                      thm_internal_status_o, thm_internal_status_ho,
+                                      thm_internal_status_selftest};
   for (auto rd : readers) {
     int r = rd(&s, reset);
     if (r != THM_OK) return r;

@@ -35,6 +35,7 @@ int thm_internal_status_wu(unsigned* s, int reset);
 int thm_internal_status_h(unsigned* s, int reset);
 int thm_internal_status_o(unsigned* s, int reset);
 int thm_internal_status_ho(unsigned* s, int reset);
+int thm_internal_status_selftest(unsigned* s, int reset);
 
 // Reads (optionally clears) a TU's status symbol.
 #define THM_STATUS_READER(fn, sym)                                                   \

@@ -94,17 +94,23 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete. Returns false (and
-// records THM_ERR_TIMEOUT) if it did not within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status) {
+// records THM_ERR_TIMEOUT) if it did not within limit_ns.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, unsigned int* status,
+                                             uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       record_status(status, THM_ERR_TIMEOUT);
       return false;
     }
   }
+}
+
+// The same with the library-wide limit kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status) {
+  return mbar_wait_ns(bar, parity, status, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------------------

@@ -7,12 +7,28 @@ stream. Nothing here computes on the CPU.
 """
 from __future__ import annotations
 
+import functools
+
 import torch
 
 from . import _lib as L
 
 BT = 64
 _ACT = {None: L.THM_ACT_NONE, "none": L.THM_ACT_NONE, "silu": L.THM_ACT_SILU}
+
+
+def _on_input_device(fn):
+    """Run the op with its first tensor argument's device current, so the
+    launch (which goes to the current device) and the pointers agree even when
+    the caller's current device is another GPU."""
+    @functools.wraps(fn)
+    def wrapped(*args, **kw):
+        t = next((a for a in args if torch.is_tensor(a)), None)
+        if t is not None and t.is_cuda and t.device.index != torch.cuda.current_device():
+            with torch.cuda.device(t.device):
+                return fn(*args, **kw)
+        return fn(*args, **kw)
+    return wrapped
 
 
 def _cuda(*ts):
@@ -27,6 +43,7 @@ def _contig(*ts):
             assert t.is_contiguous(), "inputs must be contiguous"
 
 
+@_on_input_device
 def causal_conv1d(x, weight, bias, activation=None, layout: str = "bds", l2norm_group: int = 0,
                   out=None):
     """Depthwise causal conv (kernels/causal_conv1d/kernel.py:170-230 contract).
@@ -59,6 +76,7 @@ def causal_conv1d(x, weight, bias, activation=None, layout: str = "bds", l2norm_
     return out
 
 
+@_on_input_device
 def recompute_w_u(k, v, beta, A, g, a_mode: int = 0, w=None, u=None, A_out=None):
     """w = A (k beta e^g), u = A (v beta) per 64-chunk (kernels/recompute_w_u/kernel.py:192-248).
 
@@ -85,6 +103,7 @@ def recompute_w_u(k, v, beta, A, g, a_mode: int = 0, w=None, u=None, A_out=None)
     return w, u
 
 
+@_on_input_device
 def chunk_fwd_h(k, v, g, w=None, h0=None, mode: int = 0, want_v_new: bool = False,
                 want_final: bool = False, h=None, v_new=None, h_dtype=torch.float32, want_h: bool = True):
     """Inter-chunk state recurrence (kernels/chunk_fwd_h/kernel.py:141-191).
@@ -132,6 +151,7 @@ def chunk_fwd_h(k, v, g, w=None, h0=None, mode: int = 0, want_v_new: bool = Fals
     return h
 
 
+@_on_input_device
 def chunk_fwd_o(q, k, v, g, h, scale: float, o=None):
     """Chunkwise output (kernels/chunk_fwd_o/kernel.py:146-212)."""
     _cuda(q, k, v, g, h)
@@ -153,6 +173,7 @@ def chunk_fwd_o(q, k, v, g, h, scale: float, o=None):
     return o
 
 
+@_on_input_device
 def gated_delta_fwd_ho(q, k, w, u, g, scale: float, h0=None, want_final: bool = False, o=None):
     """chunk_fwd_h (delta rule) and chunk_fwd_o fused in one kernel: returns
     (o, final state or None). Same result as
@@ -181,6 +202,7 @@ def gated_delta_fwd_ho(q, k, w, u, g, scale: float, h0=None, want_final: bool = 
     return o, final
 
 
+@_on_input_device
 def sp_prefix_fold(Ms, Ss, x0=None, nout: int | None = None, out=None):
     """States entering consecutive segments: out[0] = x0 (or 0), out[r+1] =
     Ms[r] out[r] + Ss[r]. Ms [R, BH, K, K], Ss [R, BH, K, V], x0 [BH, K, V] fp32;
@@ -204,6 +226,7 @@ def sp_prefix_fold(Ms, Ss, x0=None, nout: int | None = None, out=None):
     return out
 
 
+@_on_input_device
 def build_A(k, beta, g, sign: int = -1, out=None):
     """Per-chunk WY matrix A = (I + sign*M)^-1, M = strict_tril(beta_i k_i.k_j e^{g_i-g_j})
     (kernels/recompute_w_u/reference.py:48-91 ``_build_A`` is sign = -1). Returns
@@ -224,6 +247,7 @@ def build_A(k, beta, g, sign: int = -1, out=None):
     return out
 
 
+@_on_input_device
 def chunk_local_cumsum(g_inc, scale: float = 1.0, out=None):
     """g[b, c*64+i, h] = scale * sum_{j<=i} g_inc[b, c*64+j, h] per 64-token chunk: the
     chunk-local cumulative gate the reference's generators build

@@ -42,15 +42,28 @@ _CONST: dict = {}
 
 def _constants(k):
     """The zero u and identity h0 of the M summary for k's shape, kept across calls
-    (read-only inputs of the kernel, so one copy per shape and device serves all)."""
+    (read-only inputs of the kernel, so one copy per shape and device serves all).
+
+    The zero u is as large as k (512 MiB at B = 1, T = 131072, H = 16, K = 128
+    in bf16), so at most two shapes are kept; ``release_constants()`` frees them.
+    Before an entry is dropped the device is synchronized, so no kernel still in
+    flight on any stream reads memory the caching allocator hands out again."""
     B, T, H, K = k.shape
     key = (tuple(k.shape), k.dtype, k.device)
     if key not in _CONST:
-        if len(_CONST) > 8:
-            _CONST.clear()
+        if len(_CONST) >= 2:
+            release_constants()
         _CONST[key] = (torch.zeros_like(k),
                        torch.eye(K, device=k.device, dtype=torch.float32).expand(B, H, K, K).contiguous())
     return _CONST[key]
+
+
+def release_constants():
+    """Free the cached M-summary constants (after the kernels using them are done)."""
+    for (shape, dtype, dev) in list(_CONST):
+        if dev.type == "cuda":
+            torch.cuda.synchronize(dev)
+    _CONST.clear()
 
 
 def segment_summary(k, w, u, g):
