@@ -54,19 +54,27 @@ def test_fused_matches_oracle(with_h0, T):
 
 
 def test_fused_matches_separate_ops():
-    """Same roundings as chunk_fwd_h (bf16 h, v_new) -> chunk_fwd_o: near-identical o."""
+    """The fused kernel against chunk_fwd_h (bf16 h, v_new stored) -> chunk_fwd_o on
+    the same inputs, and both against the oracle. The fused kernel folds the decay of
+    the causal term into the tile U also uses (e^{g_t - g_s} split into a column factor
+    on v_new and a row factor on o), so the two agree to rounding, not bit for bit;
+    the state path is the same arithmetic."""
     from theorem_b200 import ops
     B, T, H = 2, 1024, 4
-    q, k, w, u, g, h0 = (t.to(DEV) for t in _inputs(B, T, H, seed=77))
+    qc, kc, wc, uc, gc, h0c = _inputs(B, T, H, seed=77)
+    q, k, w, u, g, h0 = (t.to(DEV) for t in (qc, kc, wc, uc, gc, h0c))
     scale = 128 ** -0.5
     o, fin = ops.gated_delta_fwd_ho(q, k, w, u, g, scale, h0=h0, want_final=True)
     h, vn, fin2 = ops.chunk_fwd_h(k, u, g, w=w, h0=h0, mode=1, want_v_new=True, want_final=True,
                                   h_dtype=torch.bfloat16)
     o2 = ops.chunk_fwd_o(q, k, vn, g, h, scale)
-    d = (o.float() - o2.float()).abs()
-    assert float(d.max()) <= 1e-2 * float(o2.float().abs().max()) + 1e-3, float(d.max())
-    assert float(d.mean()) <= 1e-3 * float(o2.float().abs().mean()) + 1e-5, float(d.mean())
+    assert_close(o.float().cpu(), o2.float().cpu(), TOL, TOL, "o fused vs separate")
     assert torch.allclose(fin, fin2, rtol=1e-4, atol=1e-5)
+    for b, hh in [(0, 0), (1, 3)]:
+        sl = lambda t: t[b:b + 1, :, hh:hh + 1]  # noqa: E731
+        ro, _ = _oracle(sl(qc), sl(kc), sl(wc), sl(uc), sl(gc), h0c[b:b + 1, hh:hh + 1], scale)
+        assert_close(o[b:b + 1, :, hh:hh + 1].float().cpu().double(), torch.from_numpy(ro), TOL, TOL, "o fused")
+        assert_close(o2[b:b + 1, :, hh:hh + 1].float().cpu().double(), torch.from_numpy(ro), TOL, TOL, "o separate")
 
 
 def test_many_chunks_sampled():

@@ -13,11 +13,18 @@
 //   [X; G] = [w; q] h_c                  tcgen05 M=128, N=128, K=128
 //   [.; S] = [w; q] k^T                  tcgen05 M=128, N=64,  K=128 (rows 64..127)
 //   v_new  = u - X                        rows t on TMEM lanes 0..63
-//   P      = tril(S * e^{g_t - g_s})      rows t on TMEM lanes 64..127
-//   U      = k^T (v_new e^{g_last - g_t}) tcgen05 M=128, N=128, K=64
-//   [.; L] = [. ; P] v_new                tcgen05 M=128, N=128, K=64 (rows 64..127)
+//   V''    = v_new e^{g_last - g_t}       the B operand of U (and of L, below)
+//   U      = k^T V''                      tcgen05 M=128, N=128, K=64
+//   [.; L] = [. ; tril(S)] V''            tcgen05 M=128, N=128, K=64 (rows 64..127)
 //   h_{c+1} = e^{g_last} h_c + U          registers
-//   o_c    = scale (L + e^{g_t} G)        rows t on TMEM lanes 64..127 -> TMA store
+//   o_c    = scale (e^{g_t - g_last} L + e^{g_t} G)   rows t on lanes 64..127 -> TMA store
+//
+// tril(S) V'' e^{g_t - g_last} is the causal term tril(S e^{g_t - g_s}) v_new with the
+// decay split into a column factor (folded into V'', which U needs anyway) and a row
+// factor applied in fp32 in the epilogue, so the v_new warps write one tile and P
+// needs no exponentials. Both factors stay within e^{60} while the chunk's gates span
+// at most 60 ("plain" chunks, all of BASELINE's); a chunk whose gates span more takes
+// the direct form: P = tril(S e^{g_t - g_s}) and L = P v_new with v_new as its own tile.
 //
 // w and q of a chunk sit in shared memory as one stacked [w; q] K-major tile,
 // so X and G (and S) are single M=128 products: full-rate tensor-core shapes
@@ -25,9 +32,12 @@
 // once. With M=128 accumulators row t lives on TMEM lane t (X) or 64+t (G, S,
 // L), so the math warps split by subpartition: the warps on lanes 0..63 form
 // v_new (the state path) while the warps on lanes 64..127 write the previous
-// chunk's output and form P. Arithmetic matches the separate kernels of the
-// chain: the state is rounded to bf16 only as an MMA operand (as the chain's
-// bf16 h) and v_new once to bf16 (as the chain's stored v_new).
+// chunk's output and form P. The state is carried in fp32 and rounded to bf16
+// only as an MMA operand, v_new once to bf16 (its decayed copy).
+//
+// Shared memory carries about 330 KB per chunk (the operand reads of the four
+// products, the TMA stage, the tiles the math warps write), some 1.3 us of its 128 B
+// per clock: the v_new warps write one tile, not two.
 //
 // TMEM (512 columns): U [0,128) | [X; G] of chunk parity 0 [128,256) and 1
 // [256,384) | L [384,512), shared with S [384,448) (S(c+1) is written once the
@@ -49,6 +59,7 @@ constexpr int kK = 128;
 constexpr int kV = 128;
 constexpr int kMath = 256;            // 8 math warps: 4 on TMEM lanes 0..63, 4 on lanes 64..127
 constexpr int kThreads = kMath + 64;  // + tcgen05 issuer warp + TMA producer warp
+constexpr float kPlainSpan = 60.f;    // gate span up to which a chunk takes the one-tile form
 
 struct Layout {
   static constexpr int TILE = kBT * 128 * 2;  // [64 x 128] bf16 = two 8 KB boxes
@@ -61,8 +72,9 @@ struct Layout {
   static constexpr int OFF_P = OFF_VN + TILE;         // [pad 8 KB; P [64 x 64] bf16]
   static constexpr int OFF_O = OFF_P + 2 * kBT * kBT * 2;  // o staging [64 x 128] bf16
   static constexpr int OFF_MISC = OFF_O + TILE;
-  // misc: sG [3][64] | scale e^{g} [2][64] | e^{g_m - g_s} [64] | barriers, TMEM slot
-  static constexpr int SMEM = OFF_MISC + 2048 + 1024;
+  // misc: sG [3][64] | scale e^{g_t} [2][64] | e^{g_m - g_s} [64] | output factor of L [2][64] |
+  //       plain-chunk flags [2] | barriers, TMEM slot
+  static constexpr int SMEM = OFF_MISC + 2304 + 1024;
 };
 
 __device__ __forceinline__ float2 bf2_to_f2(uint32_t x) {
@@ -87,7 +99,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* sG = reinterpret_cast<float*>(sm + Ly::OFF_MISC);           // [3][64] gates, ring
   float* sEg = reinterpret_cast<float*>(sm + Ly::OFF_MISC + 768);    // [2][64] scale e^{g_t}
   float* sEb = reinterpret_cast<float*>(sm + Ly::OFF_MISC + 1280);   // [64] e^{g_m - g_s} of the chunk
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::OFF_MISC + 1536);
+  float* sEr = reinterpret_cast<float*>(sm + Ly::OFF_MISC + 1536);   // [2][64] factor of L in o
+  int* sPlain = reinterpret_cast<int*>(sm + Ly::OFF_MISC + 2048);    // [2] chunk gates span <= kPlainSpan
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::OFF_MISC + 2064);
   uint64_t* full = bars;          // [2] TMA stage landed
   uint64_t* s_ready = bars + 2;   // h_c copied to smem (one arrival per math warp)
   uint64_t* vn_ready = bars + 3;  // v_new in smem (one arrival per lane-0..63 warp)
@@ -200,13 +214,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(bar_s);
         last_bar = bar_s;
-        // U = k^T (v_new e^{g_last - g_t})
+        // U = k^T (v_new e^{g_last - g_t}): the v_new tile of a plain chunk, else the
+        // decayed copy the v_new warps wrote over u
         if (!mbar_wait(vn_ready, ph, &g_status_ho)) { ok = false; break; }
         tc_fence_after();
+        const uint32_t vd = sPlain[st] ? sbase + Ly::OFF_VN : stg + Ly::OFF_U;
 #pragma unroll
         for (int q = 0; q < kBT / 16; ++q)
           mma_bf16_ss(tU, make_sdesc(stg + Ly::OFF_K + q * 2048, 8192, 1024),
-                      make_sdesc(stg + Ly::OFF_U + q * 2048, 8192, 1024), kIdU, q > 0);
+                      make_sdesc(vd + q * 2048, 8192, 1024), kIdU, q > 0);
         mma_commit(bar_u);
         last_bar = bar_u;
         // [.; L] = [pad; P] v_new (P has read S)
@@ -245,33 +261,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
 
-    // o of chunk j (lane-64..127 warps): row t, this warp's 64 columns.
+    // o of chunk j (lane-64..127 warps): row t, this warp's 64 columns, staged in shared
+    // memory and written by one TMA store (stores straight from registers would send 32
+    // rows per warp instruction through the L1 pipeline the shared-memory traffic uses).
     auto epilogue = [&](int j) {
       if (gidx == 0) bulk_wait_group_read0();  // the previous o tile has left the staging buffer
       named_bar_sync(3, kMath / 2);
       tc_fence_after();
-      const float e = sEg[(j & 1) * 64 + t];
+      const float eg = sEg[(j & 1) * 64 + t];
+      const float el = sEr[(j & 1) * 64 + t];
       uint8_t* ob = sm + Ly::OFF_O + half * 8192 + t * 128;
 #pragma unroll
-      for (int hq = 0; hq < 2; ++hq) {
-        float lv[32], gv[32];
-        tmem_ld32(tL + lane_row + qc + 32 * hq, lv);
-        tmem_ld32(tbase + 128 + 128 * (j & 1) + lane_row + qc + 32 * hq, gv);
+      for (int hq = 0; hq < 4; ++hq) {
+        float lv[16], gv[16];
+        tmem_ld16(tL + lane_row + qc + 16 * hq, lv);
+        tmem_ld16(tbase + 128 + 128 * (j & 1) + lane_row + qc + 16 * hq, gv);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 p;
+        for (int q = 0; q < 2; ++q) {
           const float* l8 = lv + 8 * q;
           const float* g8 = gv + 8 * q;
-          // scale L + e G, as packed fp32x2 (each lane an fmaf of the same operands)
-          uint32_t pk[4];
+          // el L + eg G, as packed fp32x2 (each lane an fmaf of the same operands)
+          uint32_t w4[4];
 #pragma unroll
           for (int z = 0; z < 4; ++z) {
-            const float2 r2 = __ffma2_rn(make_float2(l8[2 * z], l8[2 * z + 1]), make_float2(scale, scale),
-                                         __fmul2_rn(make_float2(g8[2 * z], g8[2 * z + 1]), make_float2(e, e)));
-            pk[z] = pack_bf16x2(r2.x, r2.y);
+            const float2 r2 = __ffma2_rn(make_float2(l8[2 * z], l8[2 * z + 1]), make_float2(el, el),
+                                         __fmul2_rn(make_float2(g8[2 * z], g8[2 * z + 1]), make_float2(eg, eg)));
+            w4[z] = pack_bf16x2(r2.x, r2.y);
           }
-          p = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<uint4*>(ob + ((uint32_t)((4 * hq + q) ^ (t & 7)) << 4)) = p;
+          *reinterpret_cast<uint4*>(ob + ((uint32_t)((2 * hq + q) ^ (t & 7)) << 4)) =
+              make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
       }
       tc_fence_before();
@@ -314,9 +332,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       const float gl = gc[kBT - 1];
       const float g_t = gc[t];
+      // A chunk is "plain" when its gates span at most kPlainSpan: then both U and L
+      // take the one tile v_new e^{g_last - g_s}, with L = tril(S) (v_new e^{g_last - g_s})
+      // and o's factor e^{g_t - g_last} on L (both within e^{kPlainSpan}); otherwise v_new
+      // and its decayed copy are separate tiles and P carries e^{g_t - g_s} itself.
+      float gmn = fminf(gc[lane], gc[lane + 32]), gmx = fmaxf(gc[lane], gc[lane + 32]);
+#pragma unroll
+      for (int m = 16; m >= 1; m >>= 1) {
+        gmn = fminf(gmn, __shfl_xor_sync(0xffffffffu, gmn, m));
+        gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, m));
+      }
+      const bool plain = gmx - gmn <= kPlainSpan;  // CTA-uniform
       if (xwarp) {
         // (2x) v_new = u - X for row t, this warp's 64 columns
-        if (tid < kBT) sEg[st * 64 + tid] = __expf(gc[tid]) * scale;
+        if (tid < kBT) {
+          sEg[st * 64 + tid] = __expf(gc[tid]) * scale;
+          sEr[st * 64 + tid] = plain ? __expf(gc[tid] - gl) * scale : scale;
+        }
+        if (tid == 0) sPlain[st] = plain ? 1 : 0;
         ok = mbar_wait(bar_a, ph, &g_status_ho) && ok;
         tc_fence_after();
         const float d = __expf(gl - g_t);
@@ -339,14 +372,19 @@ __global__ void __launch_bounds__(kThreads, 1)
               // u - x as fma(x, -1, u): the same rounding as the subtraction
               const float2 n = __ffma2_rn(make_float2(xv[8 * q + 2 * e], xv[8 * q + 2 * e + 1]),
                                           make_float2(-1.f, -1.f), u2);
-              // v_new (B operand of L) and v_new e^{g_last - g_t} (B operand of U),
-              // each rounded to bf16 once from the fp32 difference.
+              // v_new e^{g_last - g_t} (B operand of U; of L too for a plain chunk) and,
+              // for a steep chunk, v_new itself (B operand of L), each rounded to bf16 once
+              // from the fp32 difference.
               vn4[e] = pack_bf16x2(n.x, n.y);
               const float2 nd = __fmul2_rn(n, make_float2(d, d));
               us4[e] = pack_bf16x2(nd.x, nd.y);
             }
-            *reinterpret_cast<uint4*>(vrow + off) = make_uint4(vn4[0], vn4[1], vn4[2], vn4[3]);
-            *reinterpret_cast<uint4*>(uw + off) = make_uint4(us4[0], us4[1], us4[2], us4[3]);
+            if (plain) {
+              *reinterpret_cast<uint4*>(vrow + off) = make_uint4(us4[0], us4[1], us4[2], us4[3]);
+            } else {
+              *reinterpret_cast<uint4*>(vrow + off) = make_uint4(vn4[0], vn4[1], vn4[2], vn4[3]);
+              *reinterpret_cast<uint4*>(uw + off) = make_uint4(us4[0], us4[1], us4[2], us4[3]);
+            }
           }
         }
         fence_proxy_async_smem();
@@ -359,21 +397,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = mbar_wait(bar_l, (c - 1) & 1, &g_status_ho) && ok;
           epilogue(c - 1);
         }
-        // Decay e^{g_t - g_s} = e^{g_t - g_m} e^{g_m - g_s} about the middle g_m of the
-        // chunk's gate range: 64 + 1 exponentials per chunk instead of one per entry.
-        // Each factor is at most e^{range / 2}; chunks whose gates span more than 120
+        // Steep chunk: the decay e^{g_t - g_s} = e^{g_t - g_m} e^{g_m - g_s} about the middle
+        // g_m of the chunk's gate range: 64 + 1 exponentials per chunk instead of one per
+        // entry. Each factor is at most e^{range / 2}; chunks whose gates span more than 120
         // (factors past e^60) take one exponential per entry instead.
-        float mn = fminf(gc[lane], gc[lane + 32]), mx = fmaxf(gc[lane], gc[lane + 32]);
-#pragma unroll
-        for (int m = 16; m >= 1; m >>= 1) {
-          mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, m));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+        const bool factored = gmx - gmn <= 120.f;  // CTA-uniform
+        const float gm = 0.5f * (gmn + gmx);
+        float a_t = 1.f;
+        if (!plain) {
+          if (gidx < kBT) sEb[gidx] = __expf(gm - gc[gidx]);
+          named_bar_sync(3, kMath / 2);
+          a_t = __expf(g_t - gm);
         }
-        const bool factored = mx - mn <= 120.f;  // warp-uniform
-        const float gm = 0.5f * (mn + mx);
-        if (gidx < kBT) sEb[gidx] = __expf(gm - gc[gidx]);
-        named_bar_sync(3, kMath / 2);
-        const float a_t = __expf(g_t - gm);
         ok = mbar_wait(bar_s, ph, &g_status_ho) && ok;
         tc_fence_after();
         uint8_t* prow = sm + Ly::OFF_P + 8192 + t * 128;
@@ -391,7 +426,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 4; ++e) {
               const int s0 = 32 * half + 8 * q + 2 * e;
               float2 f;
-              if (factored) {
+              if (plain) {
+                f = make_float2(1.f, 1.f);
+              } else if (factored) {
                 f = __fmul2_rn(make_float2(a_t, a_t), make_float2(sEb[s0], sEb[s0 + 1]));
               } else {
                 f = make_float2(__expf(g_t - gc[s0]), __expf(g_t - gc[s0 + 1]));
