@@ -15,16 +15,20 @@
 //   v_new  = u - X                        rows t on TMEM lanes 0..63
 //   V''    = v_new e^{g_last - g_t}       the B operand of U (and of L, below)
 //   U      = k^T V''                      tcgen05 M=128, N=128, K=64
-//   [.; L] = [. ; tril(S)] V''            tcgen05 M=128, N=128, K=64 (rows 64..127)
+//   [X; D] += [0; P'] V''                 tcgen05 M=128, N=128, K=64, onto [X; G]
 //   h_{c+1} = e^{g_last} h_c + U          registers
-//   o_c    = scale (e^{g_t - g_last} L + e^{g_t} G)   rows t on lanes 64..127 -> TMA store
+//   o_c    = scale e^{g_t} D              rows t on lanes 64..127 -> TMA store
 //
-// tril(S) V'' e^{g_t - g_last} is the causal term tril(S e^{g_t - g_s}) v_new with the
-// decay split into a column factor (folded into V'', which U needs anyway) and a row
-// factor applied in fp32 in the epilogue, so the v_new warps write one tile and P
-// needs no exponentials. Both factors stay within e^{60} while the chunk's gates span
-// at most 60 ("plain" chunks, all of BASELINE's); a chunk whose gates span more takes
-// the direct form: P = tril(S e^{g_t - g_s}) and L = P v_new with v_new as its own tile.
+// with P' = e^{-g_last} tril(S): then D = G + e^{-g_t} tril(S e^{g_t - g_s}) v_new, the
+// causal term with its decay split into a column factor (folded into V'', which U needs
+// anyway) and a row factor e^{-g_t} shared with G, so one fp32 scale per row recovers o
+// without losing the smaller term. The v_new warps write one tile, P needs no
+// exponentials, the epilogue reads one accumulator, and S needs no TMEM of L's (its
+// product is issued right after [X; G] instead of after the previous epilogue). All
+// factors stay within e^{60} while a chunk's gates span at most 60 and g_last >= -60
+// ("plain" chunks, all of BASELINE's); another chunk ("steep") keeps the direct form:
+// P = tril(S e^{g_t - g_s}), L = P v_new with v_new as its own tile, L in the columns it
+// shares with S, o = scale (e^{g_t} G + L).
 //
 // w and q of a chunk sit in shared memory as one stacked [w; q] K-major tile,
 // so X and G (and S) are single M=128 products: full-rate tensor-core shapes
@@ -40,8 +44,8 @@
 // per clock: the v_new warps write one tile, not two.
 //
 // TMEM (512 columns): U [0,128) | [X; G] of chunk parity 0 [128,256) and 1
-// [256,384) | L [384,512), shared with S [384,448) (S(c+1) is written once the
-// epilogue has read L(c)). Shared memory: two 64 KB TMA stages (k, [w; q], u
+// [256,384) | S [384,448), sharing [384,512) with a steep chunk's L (S(c+1) waits
+// until the epilogue has read that L). Shared memory: two 64 KB TMA stages (k, [w; q], u
 // tiles of a chunk, 128-B swizzle) + state copy 32 KB + v_new 16 KB + [pad; P]
 // 16 KB + o 16 KB.
 #include <cuda_bf16.h>
@@ -203,8 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                       make_sdesc(sbase + Ly::OFF_S + kq * 2048, kK * 128, 1024), kIdXG, kq > 0);
         mma_commit(bar_a);
         last_bar = bar_a, last_ph = ph;
-        // [.; S] = [w; q] k^T into the L columns, once L(c-1) has been read
-        if (c > 0 && !mbar_wait(e_done, ph ^ 1, &g_status_ho)) { ok = false; break; }
+        // [.; S] = [w; q] k^T. Its columns double as a steep chunk's L: after a steep
+        // chunk S waits until the epilogue has read that L.
+        if (c > 0 && !sPlain[st ^ 1] && !mbar_wait(e_done, ph ^ 1, &g_status_ho)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kq = 0; kq < kK / 16; ++kq) {
@@ -225,13 +230,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                       make_sdesc(vd + q * 2048, 8192, 1024), kIdU, q > 0);
         mma_commit(bar_u);
         last_bar = bar_u;
-        // [.; L] = [pad; P] v_new (P has read S)
+        // [.; L] = [pad; P] V: a plain chunk's L accumulates onto G in the [X; G] buffer
+        // (the zero pad rows leave X as it is), a steep chunk's goes to its own columns
         if (!mbar_wait(p_ready, ph, &g_status_ho)) { ok = false; break; }
         tc_fence_after();
+        const bool plain_c = sPlain[st] != 0;
+        const uint32_t tLc = plain_c ? tXG : tL;
 #pragma unroll
         for (int q = 0; q < kBT / 16; ++q)
-          mma_bf16_ss(tL, make_sdesc(sbase + Ly::OFF_P + q * 32, 16, 1024),
-                      make_sdesc(sbase + Ly::OFF_VN + q * 2048, 8192, 1024), kIdL, q > 0);
+          mma_bf16_ss(tLc, make_sdesc(sbase + Ly::OFF_P + q * 32, 16, 1024),
+                      make_sdesc(sbase + Ly::OFF_VN + q * 2048, 8192, 1024), kIdL, plain_c || q > 0);
         mma_commit(bar_l);
         last_bar = bar_l;
       }
@@ -264,18 +272,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     // o of chunk j (lane-64..127 warps): row t, this warp's 64 columns, staged in shared
     // memory and written by one TMA store (stores straight from registers would send 32
     // rows per warp instruction through the L1 pipeline the shared-memory traffic uses).
+    // Plain chunk: the accumulator holds D = G + e^{-g_t} L, so o = scale e^{g_t} D;
+    // steep chunk: o = scale (e^{g_t} G + L) from two accumulators.
     auto epilogue = [&](int j) {
       if (gidx == 0) bulk_wait_group_read0();  // the previous o tile has left the staging buffer
       named_bar_sync(3, kMath / 2);
       tc_fence_after();
+      const bool plain_j = sPlain[j & 1] != 0;
       const float eg = sEg[(j & 1) * 64 + t];
       const float el = sEr[(j & 1) * 64 + t];
+      const uint32_t tD = tbase + 128 + 128 * (j & 1) + lane_row + qc;
       uint8_t* ob = sm + Ly::OFF_O + half * 8192 + t * 128;
 #pragma unroll
       for (int hq = 0; hq < 4; ++hq) {
-        float lv[16], gv[16];
-        tmem_ld16(tL + lane_row + qc + 16 * hq, lv);
-        tmem_ld16(tbase + 128 + 128 * (j & 1) + lane_row + qc + 16 * hq, gv);
+        float gv[16], lv[16];
+        tmem_ld16(tD + 16 * hq, gv);
+        if (!plain_j) {
+          tmem_ld16(tL + lane_row + qc + 16 * hq, lv);
+        } else {
+#pragma unroll
+          for (int z = 0; z < 16; ++z) lv[z] = 0.f;
+        }
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           const float* l8 = lv + 8 * q;
@@ -342,12 +359,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         gmn = fminf(gmn, __shfl_xor_sync(0xffffffffu, gmn, m));
         gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, m));
       }
-      const bool plain = gmx - gmn <= kPlainSpan;  // CTA-uniform
+      const bool plain = gmx - gmn <= kPlainSpan && gl >= -kPlainSpan;  // CTA-uniform
       if (xwarp) {
         // (2x) v_new = u - X for row t, this warp's 64 columns
         if (tid < kBT) {
           sEg[st * 64 + tid] = __expf(gc[tid]) * scale;
-          sEr[st * 64 + tid] = plain ? __expf(gc[tid] - gl) * scale : scale;
+          sEr[st * 64 + tid] = scale;
         }
         if (tid == 0) sPlain[st] = plain ? 1 : 0;
         ok = mbar_wait(bar_a, ph, &g_status_ho) && ok;
@@ -404,6 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool factored = gmx - gmn <= 120.f;  // CTA-uniform
         const float gm = 0.5f * (gmn + gmx);
         float a_t = 1.f;
+        const float eml = __expf(-gl);  // plain chunk: P' = e^{-g_last} tril(S)
         if (!plain) {
           if (gidx < kBT) sEb[gidx] = __expf(gm - gc[gidx]);
           named_bar_sync(3, kMath / 2);
@@ -427,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int s0 = 32 * half + 8 * q + 2 * e;
               float2 f;
               if (plain) {
-                f = make_float2(1.f, 1.f);
+                f = make_float2(eml, eml);
               } else if (factored) {
                 f = __fmul2_rn(make_float2(a_t, a_t), make_float2(sEb[s0], sEb[s0 + 1]));
               } else {
