@@ -6,8 +6,11 @@
 Headline (BASELINE.json metric "per-op us + %HBM / %TC peak; chained fwd
 tokens/s at 1/2/4/8 B200"): one step = one chained gated-DeltaNet layer
 forward at BASELINE config 5 (B=16, T=8192, H=16, K=V=128, D=2048, W=4, bf16):
-causal_conv1d(+SiLU, +L2 norm) x3 -> recompute_w_u (in-kernel WY solve) ->
-chunk_fwd_h (delta rule) + chunk_fwd_o. The 16 sequences are split over the N
+causal_conv1d(+SiLU, +L2 norm) on the q and k projections -> recompute_w_u with
+the v projection's conv+SiLU folded in (in-kernel WY solve; v never reaches HBM)
+-> chunk_fwd_h (delta rule) + chunk_fwd_o as one fused kernel (``--unfused``: the
+v conv, recompute_w_u, chunk_fwd_h and chunk_fwd_o as separate launches). The 16
+sequences are split over the N
 ranks (16/N each: strong scaling, no collective on the data path); ``value`` =
 131072 tokens / step time, timed with CUDA events between a barrier +
 synchronize, max over ranks. Inputs are >= 0.2 GB per step per GPU (> L2), so no
@@ -155,6 +158,8 @@ def chain_bytes(B, T, H, K, V, W):
     return {
         "causal_conv1d": 2 * act_k + H * K * (W + 1) * 4,          # one of q / k (v: same with V)
         "recompute_w_u": 2 * act_k + 2 * act_v + 2 * rows * 4,      # k,v in; w,u out; beta,g
+        # k, raw v projection in; w, u out; beta, g; the v conv's weights (v never stored)
+        "recompute_w_u_conv": 2 * act_k + 2 * act_v + 2 * rows * 4 + H * V * (W + 1) * 4,
         "chunk_fwd_h": 2 * act_k + act_v + rows * 4 + hbytes + act_v,  # k,w,u,g in; h, v_new out
         "chunk_fwd_o": 2 * act_k + act_v + rows * 4 + hbytes + act_v,  # q,k,v_new,g,h in; o out
         "gated_delta_ho": 3 * act_k + act_v + rows * 4 + act_v,       # q,k,w,u,g in; o out (fused h + o)
@@ -193,8 +198,9 @@ def run_chain(args, rank, world, device, B, steps, sample_clocks=True):
     xq, xk, xv, cw, cb, beta, gate = chain_inputs(B, T, H, K, V, W, 1234 + rank, device, torch.bfloat16)
     layer = GatedDeltaNetForward(H, K, V, cw, cb, fused=not args.unfused)
     fused = layer.uses_fused(torch.bfloat16)
-    names = (("causal_conv1d_x3", "recompute_w_u", "gated_delta_ho") if fused else
+    names = (("causal_conv1d_x2", "recompute_w_u_conv", "gated_delta_ho") if fused else
              ("causal_conv1d_x3", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"))
+    launches = 4 if fused else 6
     o = torch.empty(B, T, H, V, device=device, dtype=torch.bfloat16)
     stream = torch.cuda.current_stream()
 
@@ -208,14 +214,18 @@ def run_chain(args, rank, world, device, B, steps, sample_clocks=True):
         evs[0].record(stream)
         ops.causal_conv1d(xq, layer.wq, layer.bq, "silu", "bsd", K, out=bf["q"].view(B, T, H * K))
         ops.causal_conv1d(xk, layer.wk, layer.bk, "silu", "bsd", K, out=bf["k"].view(B, T, H * K))
+        if fused:
+            evs[1].record(stream)
+            w, u = ops.recompute_w_u_conv(bf["k"], xv, layer.wv, layer.bv, beta, gate, "silu", a_mode=1,
+                                          w=bf["w"], u=bf["u"])
+            evs[2].record(stream)
+            ops.gated_delta_fwd_ho(bf["q"], bf["k"], w, u, gate, layer.scale, o=o)
+            evs[3].record(stream)
+            return
         ops.causal_conv1d(xv, layer.wv, layer.bv, "silu", "bsd", 0, out=bf["v"].view(B, T, H * V))
         evs[1].record(stream)
         w, u = ops.recompute_w_u(bf["k"], bf["v"], beta, None, gate, a_mode=1, w=bf["w"], u=bf["u"])
         evs[2].record(stream)
-        if fused:
-            ops.gated_delta_fwd_ho(bf["q"], bf["k"], w, u, gate, layer.scale, o=o)
-            evs[3].record(stream)
-            return
         h, vn, _ = ops.chunk_fwd_h(bf["k"], u, gate, w=w, mode=1, h=bf["h"], v_new=bf["v"])
         evs[3].record(stream)
         ops.chunk_fwd_o(bf["q"], bf["k"], vn, gate, h, layer.scale, o=o)
@@ -248,7 +258,7 @@ def run_chain(args, rank, world, device, B, steps, sample_clocks=True):
     status = _lib.device_status()
     assert status == 0, f"in-kernel wait timed out (status {status})"
     return dict(ms=ms, per_op_ms=per, clocks=clocks, tokens_per_rank=B * T, layer=layer,
-                inputs=(xq, xk, xv, beta, gate), out=o, launches_per_step=len(names) + 2, fused=fused)
+                inputs=(xq, xk, xv, beta, gate), out=o, launches_per_step=launches, fused=fused)
 
 
 def run_e2e(args, device, layer, inputs, tokens_total):
@@ -505,6 +515,8 @@ def profile_op(args) -> int:
         "causal_conv1d_bds": lambda: ops.causal_conv1d(xb, cw[0], cb[0], "silu", "bds"),
         "chunk_fwd_o_hf32": lambda: ops.chunk_fwd_o(q, k, vn, gate, h32, K ** -0.5),
         "recompute_w_u": lambda: ops.recompute_w_u(k, v, beta, None, gate, a_mode=1, w=w, u=u),
+        "recompute_w_u_conv": lambda: ops.recompute_w_u_conv(k, xv, cw[2], cb[2], beta, gate, "silu", a_mode=1,
+                                                             w=w, u=u),
         "chunk_fwd_h": lambda: ops.chunk_fwd_h(k, u, gate, w=w, mode=1, h=h, v_new=vn),
         "chunk_fwd_o": lambda: ops.chunk_fwd_o(q, k, vn, gate, h, K ** -0.5),
         "gated_delta_ho": lambda: ops.gated_delta_fwd_ho(q, k, w, u, gate, K ** -0.5),
@@ -634,8 +646,9 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--unfused", action="store_true",
-                    help="run chunk_fwd_h -> chunk_fwd_o as two kernels instead of the fused gated_delta_ho")
-    ap.add_argument("--op", choices=["causal_conv1d", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o",
+                    help="run the v conv, recompute_w_u, chunk_fwd_h and chunk_fwd_o as separate kernels "
+                         "instead of recompute_w_u with the v conv folded in and the fused gated_delta_ho")
+    ap.add_argument("--op", choices=["causal_conv1d", "recompute_w_u", "recompute_w_u_conv", "chunk_fwd_h", "chunk_fwd_o",
                                      "chunk_fwd_o_hf32", "causal_conv1d_bds", "gated_delta_ho"],
                     help="profiling mode: launch one op (bf16, chain settings) --iters times and exit")
     ap.add_argument("--shape", default="2,4096,16,128,128", help="B,T,H,K,V for --op")
@@ -713,8 +726,8 @@ def main(argv=None) -> int:
     value = B * T / (ms / 1e3)
     by = chain_bytes(Bl, T, H, K, V, W)
     per_ms = res["per_op_ms"]
-    per_launch = {("causal_conv1d" if n == "causal_conv1d_x3" else n): (v / 3 if n == "causal_conv1d_x3" else v)
-                  for n, v in per_ms.items()}
+    per_launch = {("causal_conv1d" if n.startswith("causal_conv1d_x") else n):
+                  (v / int(n[-1]) if n.startswith("causal_conv1d_x") else v) for n, v in per_ms.items()}
     dom = max(per_launch, key=lambda n: per_launch[n])
     dom_ms = per_launch[dom]
     achieved = by[dom] / (dom_ms * 1e-3) / 1e9
@@ -722,8 +735,11 @@ def main(argv=None) -> int:
     tf = ROOT / "profiles" / "dram_traffic.json"
     if tf.exists() and world == 1:
         traffic = json.loads(tf.read_text()).get(f"chain_{dom}")
-    chain_step_bytes = 2 * by["causal_conv1d"] + (2 * Bl * T * H * V * 2 + H * V * (W + 1) * 4) + \
-        by["recompute_w_u"] + sum(by[n] for n in per_ms if n in ("chunk_fwd_h", "chunk_fwd_o", "gated_delta_ho"))
+    # q, k convs; the v conv as its own launch only on the unfused path
+    chain_step_bytes = 2 * by["causal_conv1d"] + sum(by[n] for n in per_ms if n in (
+        "recompute_w_u", "recompute_w_u_conv", "chunk_fwd_h", "chunk_fwd_o", "gated_delta_ho"))
+    if not res["fused"]:
+        chain_step_bytes += 2 * Bl * T * H * V * 2 + H * V * (W + 1) * 4
     flops = chain_flops(Bl, T, H, K, V)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -735,8 +751,9 @@ def main(argv=None) -> int:
                                   f"({Bl} per rank); no collective on the data path",
                    "l2": f"inputs {Bl * T * (3 * H * K * 2 + 8 * H) / 1e9:.2f} GB per step per GPU "
                          f"(> 126 MB L2, no flush needed)",
-                   "deltanet_kernels": ("recompute_w_u -> gated_delta_ho (chunk_fwd_h + chunk_fwd_o fused)"
-                                        if res["fused"] else "recompute_w_u -> chunk_fwd_h -> chunk_fwd_o")},
+                   "deltanet_kernels": ("recompute_w_u with the v conv folded in -> gated_delta_ho "
+                                        "(chunk_fwd_h + chunk_fwd_o fused)" if res["fused"] else
+                                        "v conv -> recompute_w_u -> chunk_fwd_h -> chunk_fwd_o")},
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": pk["hbm"], "unit": "GB/s",
                      "frac": achieved / pk["hbm"], "traffic": traffic, "peak_source": pk["src"],
                      "algorithmic_bytes_per_launch": by[dom], "avg_launch_ms": dom_ms},

@@ -79,6 +79,25 @@ int thm_recompute_w_u_fwd(const void* k, const void* v, const float* beta, const
                           int a_mode, thm_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * recompute_w_u with the v projection's conv folded in -- replaces the pair
+ * kernels/causal_conv1d (kernel.py:170-230, on the v projection, activation
+ * as given, no norm) -> kernels/recompute_w_u/kernel.py:192-248, which the
+ * layer chains (docs/ARCHITECTURE.md:200-235) with v read only by the second.
+ *
+ *   v = act(conv_b + sum_k conv_w[:, k] * xv[t - 3 + k])  (causal, zero before
+ *   each sequence's first token), then w, u as thm_recompute_w_u_fwd with
+ *   a_mode +1 / -1; v itself is never written. xv [B,T,H*V] bf16 (the layer's
+ *   channel-last projection), conv_w [H*V, 4], conv_b [H*V] fp32; k, beta, g,
+ *   w, u, A_out as thm_recompute_w_u_fwd. v equals thm_causal_conv1d_fwd's
+ *   bf16 output bit for bit, so w and u equal the two-launch path's.
+ * bf16 only; conv_width 4; T % 64 == 0; K, V in {64, 128}.
+ * ------------------------------------------------------------------------- */
+int thm_recompute_w_u_conv_fwd(const void* k, const void* xv, const float* conv_w, const float* conv_b,
+                               const float* beta, const float* g, void* w, void* u, float* A_out, int B, int T,
+                               int H, int K, int V, int conv_width, int activation, int a_mode,
+                               thm_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * build_A -- the upstream producer of recompute_w_u's A
  * (kernels/recompute_w_u/reference.py:48-91, `_build_A`), for callers that
  * pass A to thm_recompute_w_u_fwd with a_mode 0.

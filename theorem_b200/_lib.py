@@ -34,6 +34,7 @@ _SIGNATURES = {
     "thm_recompute_w_u_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
     "thm_chunk_fwd_h_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P],
     "thm_chunk_fwd_o_fwd": [_P, _P, _P, _P, _P, _P, _F, _I, _I, _I, _I, _I, _I, _I, _P],
+    "thm_recompute_w_u_conv_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P],
     "thm_build_A_fwd": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
     "thm_chunk_local_cumsum_fwd": [_P, _P, _I, _I, _I, _F, _P],
     "thm_gated_delta_fwd_ho": [_P, _P, _P, _P, _P, _P, _P, _P, _F, _I, _I, _I, _I, _I, _I, _P],

@@ -403,12 +403,20 @@ int dispatch(const void* k, const void* v, const float* beta, const float* A, co
 namespace ws {
 
 constexpr int kThreads = 320;
+constexpr int kThreadsConv = 384;  // + 2 warps forming v from the raw projection (CONV)
 constexpr int kGroup = 128;
 constexpr int kStages = 3;
+constexpr int kConvW = 4;          // causal conv width of the fused v path
+constexpr int kRawRows = 64 + kConvW - 1;  // a unit's rows plus the conv's history
+constexpr int kRawBox = 72 * 128;  // 64-channel box of kRawRows rows, padded to 1024-B atoms
 
-template <int K, int V>
+// CONV: the stage holds the raw projection x_v (rows t-3 .. t+63 of the unit, zero before the
+// sequence start) instead of v; the conv warps overwrite rows 0..63 of it with
+// v = act(conv(x_v)) before the U product reads them.
+template <int K, int V, bool CONV = false>
 struct Layout {
-  static constexpr int KB = 64 * K * 2, VB = 64 * V * 2;
+  static constexpr int KB = 64 * K * 2, VB = CONV ? (V / 64) * kRawBox : 64 * V * 2;
+  static constexpr int VLBO = CONV ? kRawBox : 8192;    // stride of v's 64-column blocks
   static constexpr int STAGE = KB + VB;
   static constexpr int OFF_STAGE = 0;                    // [3] k | v
   static constexpr int OFF_GRP = kStages * STAGE;        // per math group:
@@ -428,11 +436,11 @@ struct Layout {
 
 // W (lane 0) and U (lane 16) are M=64 accumulators interleaved in the same
 // TMEM columns; the epilogue reads both with one 32x32b load per 32 columns.
-template <int K, int V>
+template <int K, int V, bool CONV>
 __device__ __forceinline__ void wu_epilogue(uint8_t* gb, uint32_t tbase, int grp, int sp, int lane, int mt,
                                             uint64_t* tfree_o, const CUtensorMap* tm_w, const CUtensorMap* tm_u,
                                             int hh, int row0, uint32_t bar_sync) {
-  using Ly = Layout<K, V>;
+  using Ly = Layout<K, V, CONV>;
   const uint32_t tW = tbase + 256 * grp + 64 + ((uint32_t)(32 * sp) << 16);
   uint8_t* ws_ = gb + Ly::G_M;
   uint8_t* us_ = gb + Ly::G_A;
@@ -474,13 +482,14 @@ __device__ __forceinline__ void wu_epilogue(uint8_t* gb, uint32_t tbase, int grp
   }
 }
 
-template <int K, int V>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int K, int V, bool CONV>
+__global__ void __launch_bounds__(CONV ? kThreadsConv : kThreads, 1)
     recompute_w_u_ws_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_u,
                             const float* __restrict__ beta, const float* __restrict__ g,
-                            float* __restrict__ a_out, int T_len, int H, int NT, int nunits, float sgn) {
-  using Ly = Layout<K, V>;
+                            float* __restrict__ a_out, int T_len, int H, int NT, int nunits, float sgn,
+                            const float* __restrict__ conv_w, const float* __restrict__ conv_b, int silu) {
+  using Ly = Layout<K, V, CONV>;
   constexpr uint32_t kIdKK = make_idesc(1u, 64, 64, 0, 0);
   constexpr uint32_t kIdW = make_idesc(1u, 64, K, 0, 1);
   constexpr uint32_t kIdU = make_idesc(1u, 64, V, 0, 1);
@@ -497,7 +506,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* afull = bars + 10;    // [2] A operands in smem
   uint64_t* ofull = bars + 12;    // [2] W^T, U^T in TMEM
   uint64_t* tfree_o = bars + 14;  // [2] W/U region read out
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* vfull = bars + 16;    // [3] CONV: v formed in the stage (one arrival per conv warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // units of this CTA: u_i = blockIdx.x + i * gridDim.x, i < n_local
@@ -506,6 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&full[i], 33);
       mbar_init(&empty[i], 1);
+      mbar_init(&vfull[i], 2);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kfull[i], 1);
@@ -556,11 +567,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* sc = sSc + st * Ly::SC;
       if (lane == 0) {
         uint8_t* stg = sm + Ly::OFF_STAGE + st * Ly::STAGE;
-        mbar_arrive_expect_tx(&full[st], Ly::STAGE);
+        mbar_arrive_expect_tx(&full[st], CONV ? Ly::KB + (V / 64) * kRawRows * 128 : Ly::STAGE);
 #pragma unroll
         for (int j = 0; j < K / 64; ++j) tma_load_3d(stg + j * 8192, &tm_k, &full[st], j * 64, hh, row0);
 #pragma unroll
-        for (int j = 0; j < V / 64; ++j) tma_load_3d(stg + Ly::KB + j * 8192, &tm_v, &full[st], j * 64, hh, row0);
+        for (int j = 0; j < V / 64; ++j) {
+          if constexpr (CONV)  // x_v [B, T, H, V]: rows c*64-3 .. c*64+63 of sequence b
+            tma_load_4d(stg + Ly::KB + j * kRawBox, &tm_v, &full[st], j * 64, hh, c * 64 - (kConvW - 1), b);
+          else
+            tma_load_3d(stg + Ly::KB + j * 8192, &tm_v, &full[st], j * 64, hh, row0);
+        }
         if (i + 1 < n_local) {
           // the next unit's tiles into L2 now: its load is issued once a stage frees
           // (a unit later) and then comes from L2 instead of HBM
@@ -570,7 +586,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < K / 64; ++j) tma_prefetch_l2_3d(&tm_k, j * 64, hn, rn);
 #pragma unroll
-          for (int j = 0; j < V / 64; ++j) tma_prefetch_l2_3d(&tm_v, j * 64, hn, rn);
+          for (int j = 0; j < V / 64; ++j) {
+            if constexpr (CONV)
+              tma_prefetch_l2_4d(&tm_v, j * 64, hn, (bn % NT) * 64 - (kConvW - 1), bn / NT);
+            else
+              tma_prefetch_l2_3d(&tm_v, j * 64, hn, rn);
+          }
         }
       }
       // Decay e^{g_r - g_c} = e^{g_r - g_m} e^{g_m - g_c} about the middle g_m of the
@@ -625,7 +646,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (next_wu < next_kk) {
           const int i = next_wu, st = i % kStages, gi = i & 1;
           const uint32_t ph = (i >> 1) & 1;
-          if (mbar_test(&afull[gi], ph) && (i < 2 || mbar_test(&tfree_o[gi], ph ^ 1))) {
+          if (mbar_test(&afull[gi], ph) && (i < 2 || mbar_test(&tfree_o[gi], ph ^ 1)) &&
+              (!CONV || mbar_test(&vfull[st], (i / kStages) & 1))) {
             tc_fence_after();
             const uint32_t sk = sbase + Ly::OFF_STAGE + st * Ly::STAGE;
             const uint32_t sv = sk + Ly::KB;
@@ -636,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint64_t au = make_sdesc(grp + Ly::G_AU + q * 32, 16, 1024);
               // W = A_w k at TMEM lane 0, U = A_u v at lane 16 (interleaved M=64 accumulators)
               mma_bf16_ss(tbase + 256 * gi + 64, aw, make_sdesc(sk + q * 2048, 8192, 1024), kIdW, q > 0);
-              mma_bf16_ss(tbase + 256 * gi + 64 + (16u << 16), au, make_sdesc(sv + q * 2048, 8192, 1024), kIdU,
+              mma_bf16_ss(tbase + 256 * gi + 64 + (16u << 16), au, make_sdesc(sv + q * 2048, Ly::VLBO, 1024), kIdU,
                           q > 0);
             }
             mma_commit(&ofull[gi]);
@@ -658,6 +680,73 @@ __global__ void __launch_bounds__(kThreads, 1)
           __nanosleep(64);
         }
       }
+    }
+  } else if (CONV && warp >= kThreads / 32) {
+    // ---------------- conv warps (CONV) ----------------
+    // v = act(bias + sum_k w[k] x[t-3+k]) for one channel pair per thread, in place: row t of
+    // the stage's raw tile (which held x[t-3], already in this thread's window) receives
+    // v[t]. Same arithmetic as the causal_conv1d kernel's bf16 path (packed fp32x2 fmas in
+    // tap order, silu as h + h tanh(h)), so v equals that kernel's output bit for bit.
+    const int ct = tid - kThreads;  // channel pair 2 ct, 2 ct + 1 of the head
+    const bool active = ct < V / 2;
+    const uint32_t cb = (uint32_t)(ct & 31) * 4;  // byte of the pair in a 128-B row
+    for (int i = 0; i < n_local && ok; ++i) {
+      const int u = blockIdx.x + i * gridDim.x;
+      const int st = i % kStages;
+      const int hh = u % H;
+      float2 wk[kConvW], bias2 = make_float2(0.f, 0.f);
+      if (active) {
+        const long long ch = (long long)hh * V + 2 * ct;
+        bias2 = make_float2(__ldg(conv_b + ch), __ldg(conv_b + ch + 1));
+#pragma unroll
+        for (int k = 0; k < kConvW; ++k) wk[k] = make_float2(__ldg(conv_w + ch * kConvW + k), __ldg(conv_w + (ch + 1) * kConvW + k));
+      }
+      ok = __all_sync(0xffffffffu, mbar_wait(&full[st], (i / kStages) & 1, &g_status_wu));
+      if (!ok) break;
+      if (active) {
+        uint8_t* box = sm + Ly::OFF_STAGE + st * Ly::STAGE + Ly::KB + (ct >> 5) * kRawBox;
+        auto at = [&](int r) -> uint32_t* {
+          return reinterpret_cast<uint32_t*>(box + r * 128 + (((cb >> 4) ^ (uint32_t)(r & 7)) << 4) + (cb & 15));
+        };
+        auto ld2 = [&](int r) {
+          const uint32_t x = *at(r);
+          return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x));
+        };
+        // Rows in batches of 8: the batch's raw rows t0+3 .. t0+10 are read before rows
+        // t0 .. t0+7 are overwritten, so loads, the 8 independent outputs and the stores
+        // pipeline instead of each step waiting on the previous one's store.
+        constexpr int kBatch = 8;
+        float2 xw[kConvW - 1 + kBatch];
+#pragma unroll
+        for (int r = 0; r < kConvW - 1; ++r) xw[r] = ld2(r);
+#pragma unroll 1
+        for (int t0 = 0; t0 < 64; t0 += kBatch) {
+#pragma unroll
+          for (int r = 0; r < kBatch; ++r) xw[kConvW - 1 + r] = ld2(t0 + kConvW - 1 + r);
+          uint32_t outp[kBatch];
+#pragma unroll
+          for (int r = 0; r < kBatch; ++r) {
+            float2 acc = bias2;
+#pragma unroll
+            for (int k = 0; k < kConvW; ++k) acc = __ffma2_rn(xw[r + k], wk[k], acc);
+            if (silu) {
+              const float2 h = __fmul2_rn(make_float2(0.5f, 0.5f), acc);
+              float t0h, t1h;
+              asm("tanh.approx.f32 %0, %1;" : "=f"(t0h) : "f"(h.x));
+              asm("tanh.approx.f32 %0, %1;" : "=f"(t1h) : "f"(h.y));
+              acc = __ffma2_rn(h, make_float2(t0h, t1h), h);
+            }
+            outp[r] = pack_bf16x2(acc.x, acc.y);
+          }
+#pragma unroll
+          for (int r = 0; r < kBatch; ++r) *at(t0 + r) = outp[r];
+#pragma unroll
+          for (int r = 0; r < kConvW - 1; ++r) xw[r] = xw[kBatch + r];
+        }
+      }
+      fence_proxy_async_smem();  // the tensor core reads v through the async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&vfull[st]);
     }
   } else {
     // ---------------- math groups ----------------
@@ -908,7 +997,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(bar_sync, kGroup);  // sA / sM reads done before they become staging
       if (has_prev) {
         tc_fence_after();
-        wu_epilogue<K, V>(gb, tbase, grp, sp, lane, mt, tfree_o, &tm_w, &tm_u, prev_hh, prev_row0, bar_sync);
+        wu_epilogue<K, V, CONV>(gb, tbase, grp, sp, lane, mt, tfree_o, &tm_w, &tm_u, prev_hh, prev_row0, bar_sync);
       }
       has_prev = true;
       prev_hh = hh;
@@ -922,7 +1011,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         if (mt == 0) bulk_wait_group_read0();
         named_bar_sync(bar_sync, kGroup);
-        wu_epilogue<K, V>(gb, tbase, grp, sp, lane, mt, tfree_o, &tm_w, &tm_u, prev_hh, prev_row0, bar_sync);
+        wu_epilogue<K, V, CONV>(gb, tbase, grp, sp, lane, mt, tfree_o, &tm_w, &tm_u, prev_hh, prev_row0, bar_sync);
       } else {
         ok = false;
       }
@@ -936,10 +1025,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tmem_dealloc(tbase, 512);
 }
 
-template <int K, int V>
+// conv_w == nullptr: v is given. Else v is the raw projection x_v [B, T, H, V] and the
+// kernel forms v = act(causal_conv1d(x_v, conv_w, conv_b)) (width kConvW) itself.
+template <int K, int V, bool CONV>
 int launch(const void* k, const void* v, const float* beta, const float* g, void* w, void* u, float* a_out, int B,
-           int T_len, int H, int a_mode, cudaStream_t st) {
-  using Ly = Layout<K, V>;
+           int T_len, int H, int a_mode, const float* conv_w, const float* conv_b, int silu, cudaStream_t st) {
+  using Ly = Layout<K, V, CONV>;
   const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int NT = T_len / 64;
   const uint64_t rows = (uint64_t)B * T_len;
@@ -955,17 +1046,26 @@ int launch(const void* k, const void* v, const float* beta, const float* g, void
   {
     uint64_t dims[3] = {(uint64_t)V, (uint64_t)H, rows};
     uint64_t str[2] = {(uint64_t)V * 2, (uint64_t)H * V * 2};
-    int r = encode_tiled(&tv, dt, 3, v, dims, str, box);
-    if (r == THM_OK) r = encode_tiled(&tu, dt, 3, u, dims, str, box);
+    int r = encode_tiled(&tu, dt, 3, u, dims, str, box);
+    if (r == THM_OK) {
+      if constexpr (CONV) {
+        const uint64_t dims4[4] = {(uint64_t)V, (uint64_t)H, (uint64_t)T_len, (uint64_t)B};
+        const uint64_t str4[3] = {(uint64_t)V * 2, (uint64_t)H * V * 2, (uint64_t)T_len * H * V * 2};
+        const uint32_t box4[4] = {64u, 1u, (uint32_t)kRawRows, 1u};
+        r = encode_tiled(&tv, dt, 4, v, dims4, str4, box4);
+      } else {
+        r = encode_tiled(&tv, dt, 3, v, dims, str, box);
+      }
+    }
     if (r != THM_OK) return r;
   }
-  auto kern = recompute_w_u_ws_kernel<K, V>;
+  auto kern = recompute_w_u_ws_kernel<K, V, CONV>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
     return THM_ERR_CUDA;
   const int nunits = B * NT * H;
   const int grid = nunits < sm_count() ? nunits : sm_count();
-  kern<<<grid, kThreads, Ly::SMEM, st>>>(tk, tv, tw, tu, beta, g, a_out, T_len, H, NT, nunits,
-                                         a_mode > 0 ? 1.0f : -1.0f);
+  kern<<<grid, CONV ? kThreadsConv : kThreads, Ly::SMEM, st>>>(tk, tv, tw, tu, beta, g, a_out, T_len, H, NT, nunits,
+                                                              a_mode > 0 ? 1.0f : -1.0f, conv_w, conv_b, silu);
   return check_launch();
 }
 
@@ -992,14 +1092,36 @@ extern "C" int thm_recompute_w_u_fwd(const void* k, const void* v, const float* 
   if (dtype == THM_BF16 && a_mode != 0) {
     // In-kernel A with bf16 operands: the persistent warp-specialized kernel.
     if (K == 64)
-      return V == 64 ? wu::ws::launch<64, 64>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, st)
-                     : wu::ws::launch<64, 128>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, st);
-    return V == 64 ? wu::ws::launch<128, 64>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, st)
-                   : wu::ws::launch<128, 128>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, st);
+      return V == 64 ? wu::ws::launch<64, 64, false>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, nullptr, nullptr, 0, st)
+                     : wu::ws::launch<64, 128, false>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, nullptr, nullptr, 0, st);
+    return V == 64 ? wu::ws::launch<128, 64, false>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, nullptr, nullptr, 0, st)
+                   : wu::ws::launch<128, 128, false>(k, v, beta, g, w, u, A_out, B, T, H, a_mode, nullptr, nullptr, 0, st);
   }
   if (dtype == THM_BF16)
     return wu::dispatch<__nv_bfloat16>(k, v, beta, A, g, w, u, A_out, B, T, H, K, V, a_mode, st);
   return wu::dispatch<float>(k, v, beta, A, g, w, u, A_out, B, T, H, K, V, a_mode, st);
+}
+
+extern "C" int thm_recompute_w_u_conv_fwd(const void* k, const void* xv, const float* conv_w, const float* conv_b,
+                                          const float* beta, const float* g, void* w, void* u, float* A_out, int B,
+                                          int T, int H, int K, int V, int conv_width, int activation, int a_mode,
+                                          thm_stream_t stream) {
+  using namespace thm;
+  if (B < 0 || T < 0 || H < 0 || K <= 0 || V <= 0 || T % 64 != 0) return THM_ERR_INVALID;
+  if (a_mode != 1 && a_mode != -1) return THM_ERR_INVALID;
+  if (activation != THM_ACT_NONE && activation != THM_ACT_SILU) return THM_ERR_INVALID;
+  if ((long long)B * T * H == 0) return THM_OK;
+  if (!k || !xv || !conv_w || !conv_b || !beta || !g || !w || !u) return THM_ERR_INVALID;
+  if (!(K == 64 || K == 128) || !(V == 64 || V == 128) || conv_width != wu::ws::kConvW) return THM_ERR_UNSUPPORTED;
+  if (!aligned16(k) || !aligned16(xv) || !aligned16(w) || !aligned16(u)) return THM_ERR_ALIGNMENT;
+  if ((long long)B * H > 65535) return THM_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int silu = activation == THM_ACT_SILU;
+  if (K == 64)
+    return V == 64 ? wu::ws::launch<64, 64, true>(k, xv, beta, g, w, u, A_out, B, T, H, a_mode, conv_w, conv_b, silu, st)
+                   : wu::ws::launch<64, 128, true>(k, xv, beta, g, w, u, A_out, B, T, H, a_mode, conv_w, conv_b, silu, st);
+  return V == 64 ? wu::ws::launch<128, 64, true>(k, xv, beta, g, w, u, A_out, B, T, H, a_mode, conv_w, conv_b, silu, st)
+                 : wu::ws::launch<128, 128, true>(k, xv, beta, g, w, u, A_out, B, T, H, a_mode, conv_w, conv_b, silu, st);
 }
 
 extern "C" int thm_build_A_fwd(const void* k, const float* beta, const float* g, float* A, int B, int T, int H,

@@ -104,6 +104,39 @@ def recompute_w_u(k, v, beta, A, g, a_mode: int = 0, w=None, u=None, A_out=None)
 
 
 @_on_input_device
+def recompute_w_u_conv(k, xv, conv_weight, conv_bias, beta, g, activation=None, a_mode: int = 1, w=None, u=None,
+                       A_out=None):
+    """recompute_w_u with v = act(causal_conv1d(xv)) formed in the same kernel.
+
+    The layer's v projection ``xv`` [B,T,H*V] bf16 goes through the depthwise causal
+    conv (``conv_weight`` [H*V, 4], ``conv_bias`` [H*V] fp32, optional SiLU) and straight
+    into u = A (v beta): the chain kernels/causal_conv1d -> kernels/recompute_w_u
+    (kernel.py:192-248) without v in HBM. a_mode +1 / -1 computes A in-kernel.
+    """
+    _cuda(k, xv, conv_weight, conv_bias, beta, g)
+    _contig(k, xv, conv_weight, conv_bias, beta, g)
+    B, T, H, K = k.shape
+    assert k.dtype == torch.bfloat16 and xv.dtype == torch.bfloat16, "bf16 only"
+    assert xv.dim() == 3 and xv.shape[:2] == (B, T) and xv.shape[2] % H == 0
+    V = xv.shape[2] // H
+    Dw, W = conv_weight.shape
+    assert Dw == H * V and conv_bias.shape == (H * V,)
+    assert conv_weight.dtype == torch.float32 and conv_bias.dtype == torch.float32, "conv weight/bias must be float32"
+    assert beta.shape == (B, T, H) and g.shape == (B, T, H)
+    assert beta.dtype == torch.float32 and g.dtype == torch.float32, "beta / g must be float32"
+    assert T % BT == 0, "T must be a multiple of BT (=64)"
+    assert a_mode in (1, -1), "the conv-fused path computes A in-kernel"
+    w = torch.empty_like(k) if w is None else w
+    u = torch.empty(B, T, H, V, device=k.device, dtype=k.dtype) if u is None else u
+    st = L.stream_of(k)
+    L.check(L.load().thm_recompute_w_u_conv_fwd(L.ptr(k), L.ptr(xv), L.ptr(conv_weight), L.ptr(conv_bias),
+                                                L.ptr(beta), L.ptr(g), L.ptr(w), L.ptr(u), L.ptr(A_out), B, T, H,
+                                                K, V, W, _ACT[activation], int(a_mode), st),
+            "thm_recompute_w_u_conv_fwd")
+    return w, u
+
+
+@_on_input_device
 def chunk_fwd_h(k, v, g, w=None, h0=None, mode: int = 0, want_v_new: bool = False,
                 want_final: bool = False, h=None, v_new=None, h_dtype=torch.float32, want_h: bool = True):
     """Inter-chunk state recurrence (kernels/chunk_fwd_h/kernel.py:141-191).
