@@ -20,7 +20,8 @@ Also on the line: ``weak`` (N > 1: every rank its own B=16 batch), ``e2e``
 (the same step through the public API on every rank with pinned host buffers:
 H2D of inputs and D2H of o inside the timed region, max over ranks), ``sp``
 (the sequence-parallel variant, B=1 T=131072 split along T over the ranks, with
-a check against the unsplit sequence), and on rank 0 at N=1 ``per_op``
+a check against the unsplit sequence), ``split_check`` (N > 1: every rank's o against
+the same 16 sequences in one call on rank 0, bit for bit), and on rank 0 at N=1 ``per_op``
 (configs 1-4, L2 flushed single launches and 200 back-to-back launches),
 ``roofline`` of the dominant chain kernel measured live, ``cpu_baseline`` (the
 reference's eager torch path restated in oracle/eager.py, fp32 on the host
@@ -132,16 +133,22 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # synthetic inputs (BASELINE.json distributions; N(m, s2) = mean / variance)
 # ---------------------------------------------------------------------------
+WEIGHT_SEED = 4321  # the layer's conv weights: one draw shared by every rank
+
+
 def chain_inputs(B, T, H, K, V, W, seed, device, dtype):
+    """Activations from ``seed`` (each rank its own sequences); the conv weights from
+    WEIGHT_SEED, so all ranks run the same layer."""
     import torch
     import torch.nn.functional as F
     g = torch.Generator(device=device).manual_seed(seed)
+    gw = torch.Generator(device=device).manual_seed(WEIGHT_SEED)
     D, DV = H * K, H * V
     xq = torch.randn(B, T, D, generator=g, device=device).to(dtype)
     xk = torch.randn(B, T, D, generator=g, device=device).to(dtype)
     xv = torch.randn(B, T, DV, generator=g, device=device).to(dtype)
-    cw = [torch.randn(n, W, generator=g, device=device) * 0.5 for n in (D, D, DV)]
-    cb = [torch.randn(n, generator=g, device=device) * math.sqrt(0.1) for n in (D, D, DV)]
+    cw = [torch.randn(n, W, generator=gw, device=device) * 0.5 for n in (D, D, DV)]
+    cb = [torch.randn(n, generator=gw, device=device) * math.sqrt(0.1) for n in (D, D, DV)]
     beta = torch.sigmoid(torch.randn(B, T, H, generator=g, device=device))
     inc = F.logsigmoid(torch.randn(B, T, H, generator=g, device=device)) / 16
     gate = inc.reshape(B, T // 64, 64, H).cumsum(2).reshape(B, T, H).contiguous()
@@ -261,6 +268,30 @@ def run_chain(args, rank, world, device, B, steps, sample_clocks=True):
                 inputs=(xq, xk, xv, beta, gate), out=o, launches_per_step=launches, fused=fused)
 
 
+def split_check(args, rank, world, device, res):
+    """Outside the timed region: every rank's o gathered on rank 0 against the same
+    sequences run as one batch on rank 0's GPU (each rank's inputs regenerated from its
+    seed, the shared weights). Sequences are independent in every kernel, so the split
+    must reproduce the one-GPU result bit for bit. Returns the check on rank 0, else None."""
+    import torch
+    import torch.distributed as dist
+    o = res["out"]
+    parts = [torch.empty_like(o) for _ in range(world)]
+    dist.all_gather(parts, o)
+    if rank != 0:
+        return None
+    c = CFG5
+    T, H, K, V, W = c["T"], c["H"], c["K"], c["V"], c["W"]
+    Bl = o.shape[0]
+    ins = [chain_inputs(Bl, T, H, K, V, W, 1234 + r, device, torch.bfloat16) for r in range(world)]
+    cat = [torch.cat([x[i] for x in ins], 0) for i in (0, 1, 2, 5, 6)]  # xq, xk, xv, beta, gate
+    ref, _ = res["layer"](*cat, final_state=False)
+    got = torch.cat(parts, 0)
+    diff = (got.float() - ref.float()).abs().max().item()
+    return {"what": f"o of the {world} ranks (all_gather) vs the same {world * Bl} sequences in one call on rank 0",
+            "bitwise_equal": bool(torch.equal(got, ref)), "max_abs_diff": diff}
+
+
 def run_e2e(args, device, layer, inputs, tokens_total):
     """Same step through the public API from pinned host memory, D2H of o included:
     GatedDeltaNetForward.forward_from_host, which pipelines the copies of one group
@@ -302,7 +333,7 @@ def run_e2e(args, device, layer, inputs, tokens_total):
 # ---------------------------------------------------------------------------
 # per-op configs 1-4 (rank 0, N=1)
 # ---------------------------------------------------------------------------
-def time_op(fn, iters=20, warm=3, flush=None, saturated=200):
+def time_op(fn, iters=50, warm=5, flush=None, saturated=200):
     """Flushed single launches (``iters``, L2 emptied before each) and a saturated
     mode: ``saturated`` launches back to back between two events, no flush, so
     launch latency and the kernel's ramp overlap the previous launch's tail (the
@@ -699,6 +730,10 @@ def main(argv=None) -> int:
     pk = peaks()
     extra = {}
     if world > 1:
+        chk = split_check(args, rank, world, device, res)
+        if chk is not None:
+            extra["split_check"] = chk
+        torch.cuda.empty_cache()
         # Weak scaling beside it: every rank its own full B = 16 batch.
         wk = run_chain(args, rank, world, device, B, min(args.steps, 20), sample_clocks=False)
         extra["weak"] = {"value": world * B * T / (wk["ms"] / min(args.steps, 20) / 1e3), "unit": UNIT,
