@@ -1,6 +1,7 @@
 """GPU parity of the whole gated-DeltaNet layer forward (theorem_b200.chain):
-causal_conv1d(+SiLU, +L2 norm) x3 -> recompute_w_u (in-kernel WY solve) ->
-the fused chunk_fwd_h + chunk_fwd_o kernel (or the two separate kernels),
+causal_conv1d(+SiLU, +L2 norm) on q, k -> recompute_w_u with the v conv folded in
+(in-kernel WY solve) -> the fused chunk_fwd_h + chunk_fwd_o kernel (or the v conv,
+recompute_w_u, chunk_fwd_h and chunk_fwd_o as separate kernels),
 against the float64 oracle chain (oracle.ops.gated_delta_chain) at the north
 star's bf16 tolerance rtol = atol = 1e-2 (kernels/chunk_fwd_o/task.yml, applied
 as eval.py:85-117 does through verbose_allclose).
@@ -76,3 +77,19 @@ def test_chain_config5_sampled_sequences():
                      f"o b={b} h={h}")
         assert_close(fin[b:b + 1, h:h + 1].cpu().double(), torch.from_numpy(rfin), TOL, TOL,
                      f"final b={b} h={h}")
+
+
+def test_conv_width_3_takes_the_unfused_path():
+    """The conv-folded recompute_w_u is built for conv width 4; another width runs the
+    layer through the separate conv, recompute_w_u, chunk_fwd_h and chunk_fwd_o
+    launches, still against the oracle."""
+    from theorem_b200.chain import GatedDeltaNetForward
+    B, T, H, K = 1, 192, 2, 128
+    xq, xk, xv, cw, cb, beta, g = chain_inputs(B, T, H, K, K, 3, 8, DEV)
+    layer = GatedDeltaNetForward(H, K, K, cw, cb)
+    assert not layer.uses_fused(torch.bfloat16)
+    o, fin = layer(xq, xk, xv, beta, g)
+    for h in range(H):
+        ro, rfin = _oracle_seq((xq, xk, xv), cw, cb, beta, g, 0, h, K, K)
+        assert_close(o[:, :, h:h + 1].float().cpu().double(), torch.from_numpy(ro), TOL, TOL, f"o h={h}")
+        assert_close(fin[:, h:h + 1].cpu().double(), torch.from_numpy(rfin), TOL, TOL, f"final h={h}")

@@ -89,3 +89,14 @@ def test_rejects_unsupported():
         ops.recompute_w_u_conv(k, xv, cw[:, :3].contiguous(), cb, beta, g, "silu", a_mode=1)  # width 3
     with pytest.raises(Exception):
         ops.recompute_w_u_conv(k, xv, cw, cb, beta, g, "silu", a_mode=0)
+
+
+def test_single_chunk_sequences():
+    """T = 64: every unit is a sequence start, so each reads a zero conv history (the
+    4-D TMA fills the rows before t = 0 of every sequence, not the previous one's)."""
+    from theorem_b200 import ops
+    B, T, H, K, V = 3, 64, 5, 128, 128
+    k, xv, cw, cb, beta, g = (t.to(DEV) for t in _inputs(B, T, H, K, V, seed=31))
+    w1, u1, _, _ = _two_launch(k, xv, cw, cb, beta, g, "silu", 1)
+    w2, u2 = ops.recompute_w_u_conv(k, xv, cw, cb, beta, g, "silu", a_mode=1)
+    assert torch.equal(w1, w2) and torch.equal(u1, u2)
