@@ -205,6 +205,7 @@ def run_chain(args, rank, world, device, B, steps, sample_clocks=True):
     xq, xk, xv, cw, cb, beta, gate = chain_inputs(B, T, H, K, V, W, 1234 + rank, device, torch.bfloat16)
     layer = GatedDeltaNetForward(H, K, V, cw, cb, fused=not args.unfused)
     fused = layer.uses_fused(torch.bfloat16)
+    assert fused == layer.folds_v_conv(torch.bfloat16), "config 5's conv width is 4"
     names = (("causal_conv1d_x2", "recompute_w_u_conv", "gated_delta_ho") if fused else
              ("causal_conv1d_x3", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"))
     launches = 4 if fused else 6

@@ -79,15 +79,15 @@ def test_chain_config5_sampled_sequences():
                      f"final b={b} h={h}")
 
 
-def test_conv_width_3_takes_the_unfused_path():
-    """The conv-folded recompute_w_u is built for conv width 4; another width runs the
-    layer through the separate conv, recompute_w_u, chunk_fwd_h and chunk_fwd_o
-    launches, still against the oracle."""
+def test_conv_width_3_keeps_the_v_conv_separate():
+    """The conv-folded recompute_w_u is built for conv width 4; another width runs the v
+    conv and recompute_w_u as separate launches and keeps the fused state/output kernel,
+    still against the oracle."""
     from theorem_b200.chain import GatedDeltaNetForward
     B, T, H, K = 1, 192, 2, 128
     xq, xk, xv, cw, cb, beta, g = chain_inputs(B, T, H, K, K, 3, 8, DEV)
     layer = GatedDeltaNetForward(H, K, K, cw, cb)
-    assert not layer.uses_fused(torch.bfloat16)
+    assert layer.uses_fused(torch.bfloat16) and not layer.folds_v_conv(torch.bfloat16)
     o, fin = layer(xq, xk, xv, beta, g)
     for h in range(H):
         ro, rfin = _oracle_seq((xq, xk, xv), cw, cb, beta, g, 0, h, K, K)

@@ -19,12 +19,12 @@ bf16 inputs -- the state is carried in fp32 inside chunk_fwd_h and only its
 stored per-chunk copy is rounded -- else fp32) are kept in buffers reused
 across calls with the same shape.
 
-With bf16 inputs and K = V = 128 the v conv runs inside recompute_w_u
-(ops.recompute_w_u_conv: v is read only there, so it never reaches HBM) and
-the last two steps run as one kernel (ops.gated_delta_fwd_ho): the state
-recurrence and the output share a pass over the chunks and h, v_new never
-reach HBM. ``fused=False`` keeps the separate conv, chunk_fwd_h and
-chunk_fwd_o launches.
+With bf16 inputs and K = V = 128 the last two steps run as one kernel
+(ops.gated_delta_fwd_ho): the state recurrence and the output share a pass
+over the chunks and h, v_new never reach HBM; with a conv width of 4 the v
+conv also runs inside recompute_w_u (ops.recompute_w_u_conv: v is read only
+there, so it never reaches HBM). ``fused=False`` keeps the separate v conv,
+recompute_w_u, chunk_fwd_h and chunk_fwd_o launches.
 """
 from __future__ import annotations
 
@@ -48,8 +48,12 @@ class GatedDeltaNetForward:
         self._buf: dict = {}
 
     def uses_fused(self, dtype) -> bool:
-        return (self.fused and dtype == torch.bfloat16 and self.K == 128 and self.V == 128
-                and self.wv.shape[1] == 4)
+        """chunk_fwd_h + chunk_fwd_o as the one fused kernel."""
+        return self.fused and dtype == torch.bfloat16 and self.K == 128 and self.V == 128
+
+    def folds_v_conv(self, dtype) -> bool:
+        """The v conv inside recompute_w_u (built for conv width 4)."""
+        return self.uses_fused(dtype) and self.wv.shape[1] == 4
 
     def _buffers(self, xq, xv, B, T):
         key = (B, T, xq.dtype, xq.device)
@@ -60,7 +64,7 @@ class GatedDeltaNetForward:
                 key=key,
                 q=torch.empty(B, T, H, K, device=dev, dtype=dt),
                 k=torch.empty(B, T, H, K, device=dev, dtype=dt),
-                v=None if self.uses_fused(dt) else torch.empty(B, T, H, V, device=dev, dtype=dt),
+                v=None if self.folds_v_conv(dt) else torch.empty(B, T, H, V, device=dev, dtype=dt),
                 w=torch.empty(B, T, H, K, device=dev, dtype=dt),
                 u=torch.empty(B, T, H, V, device=dev, dtype=dt),
                 h=None if self.uses_fused(dt) else torch.empty(
@@ -77,12 +81,14 @@ class GatedDeltaNetForward:
         q, k, v = bf["q"], bf["k"], bf["v"]
         ops.causal_conv1d(xq, self.wq, self.bq, self.activation, "bsd", K, out=q.view(B, T, H * K))
         ops.causal_conv1d(xk, self.wk, self.bk, self.activation, "bsd", K, out=k.view(B, T, H * K))
-        if self.uses_fused(xq.dtype):
+        if self.folds_v_conv(xq.dtype):
             w, u = ops.recompute_w_u_conv(k, xv, self.wv, self.bv, beta, g, self.activation, a_mode=1,
                                           w=bf["w"], u=bf["u"])
+        else:
+            ops.causal_conv1d(xv, self.wv, self.bv, self.activation, "bsd", 0, out=v.view(B, T, H * V))
+            w, u = ops.recompute_w_u(k, v, beta, None, g, a_mode=1, w=bf["w"], u=bf["u"])
+        if self.uses_fused(xq.dtype):
             return ops.gated_delta_fwd_ho(q, k, w, u, g, self.scale, h0=h0, want_final=final_state, o=out)
-        ops.causal_conv1d(xv, self.wv, self.bv, self.activation, "bsd", 0, out=v.view(B, T, H * V))
-        w, u = ops.recompute_w_u(k, v, beta, None, g, a_mode=1, w=bf["w"], u=bf["u"])
         h, v_new, fin = ops.chunk_fwd_h(k, u, g, w=w, h0=h0, mode=1, want_v_new=True, want_final=final_state,
                                         h=bf["h"], v_new=v)
         o = ops.chunk_fwd_o(q, k, v_new, g, h, self.scale, o=out)

@@ -1113,7 +1113,8 @@ extern "C" int thm_recompute_w_u_conv_fwd(const void* k, const void* xv, const f
   if ((long long)B * T * H == 0) return THM_OK;
   if (!k || !xv || !conv_w || !conv_b || !beta || !g || !w || !u) return THM_ERR_INVALID;
   if (!(K == 64 || K == 128) || !(V == 64 || V == 128) || conv_width != wu::ws::kConvW) return THM_ERR_UNSUPPORTED;
-  if (!aligned16(k) || !aligned16(xv) || !aligned16(w) || !aligned16(u)) return THM_ERR_ALIGNMENT;
+  if (!aligned16(k) || !aligned16(xv) || !aligned16(w) || !aligned16(u) || (A_out && !aligned16(A_out)))
+    return THM_ERR_ALIGNMENT;
   if ((long long)B * H > 65535) return THM_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int silu = activation == THM_ACT_SILU;

@@ -128,6 +128,11 @@ def recompute_w_u_conv(k, xv, conv_weight, conv_bias, beta, g, activation=None, 
     assert a_mode in (1, -1), "the conv-fused path computes A in-kernel"
     w = torch.empty_like(k) if w is None else w
     u = torch.empty(B, T, H, V, device=k.device, dtype=k.dtype) if u is None else u
+    for name, t, shape, dt in (("w", w, (B, T, H, K), k.dtype), ("u", u, (B, T, H, V), k.dtype),
+                               ("A_out", A_out, (B, T, H, BT), torch.float32)):
+        if t is not None:
+            assert t.shape == shape and t.dtype == dt, f"{name} must be {tuple(shape)} {dt}"
+            assert t.is_contiguous() and t.device == k.device, f"{name} must be contiguous on {k.device}"
     st = L.stream_of(k)
     L.check(L.load().thm_recompute_w_u_conv_fwd(L.ptr(k), L.ptr(xv), L.ptr(conv_weight), L.ptr(conv_bias),
                                                 L.ptr(beta), L.ptr(g), L.ptr(w), L.ptr(u), L.ptr(A_out), B, T, H,
