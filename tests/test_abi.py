@@ -55,3 +55,21 @@ def test_invalid_arguments_rejected_without_gpu():
     assert lib.thm_causal_conv1d_fwd(None, None, None, None, 1, 1, 1, 0, 0, 0, 0, 0, None) == _lib.THM_ERR_INVALID
     assert lib.thm_causal_conv1d_fwd(None, None, None, None, 0, 8, 8, 4, 0, 0, 0, 0, None) == _lib.THM_OK
     assert lib.thm_causal_conv1d_fwd(None, None, None, None, 1, 8, 8, 4, 7, 0, 0, 0, None) == _lib.THM_ERR_INVALID
+
+
+def test_conv_folded_recompute_w_u_rejects_arguments_without_gpu():
+    """thm_recompute_w_u_conv_fwd checks its arguments on the host, before any CUDA call:
+    only an in-kernel A (a_mode +1 / -1), a known activation, T % 64 == 0, and conv
+    width 4 with K, V in {64, 128}; an empty problem is a no-op."""
+    lib = _lib.load()
+    f = lib.thm_recompute_w_u_conv_fwd
+    fake = 1 << 20  # never dereferenced: every case returns before touching memory
+    p9 = [fake] * 9
+    ok_shape = (1, 64, 1, 128, 128, 4, 1)  # B, T, H, K, V, width, activation
+    assert f(*p9, *ok_shape, 0, None) == _lib.THM_ERR_INVALID          # a_mode 0: A is not taken
+    assert f(*p9, 1, 65, 1, 128, 128, 4, 1, 1, None) == _lib.THM_ERR_INVALID  # T % 64 != 0
+    assert f(*p9, 1, 64, 1, 128, 128, 4, 7, 1, None) == _lib.THM_ERR_INVALID  # unknown activation
+    assert f(*([None] * 9), *ok_shape, 1, None) == _lib.THM_ERR_INVALID       # null pointers
+    assert f(*([None] * 9), 0, 64, 1, 128, 128, 4, 1, 1, None) == _lib.THM_OK  # empty batch
+    assert f(*p9, 1, 64, 1, 128, 128, 3, 1, 1, None) == _lib.THM_ERR_UNSUPPORTED  # conv width 3
+    assert f(*p9, 1, 64, 1, 96, 128, 4, 1, -1, None) == _lib.THM_ERR_UNSUPPORTED  # K = 96
