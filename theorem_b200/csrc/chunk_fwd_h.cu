@@ -241,8 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // v_new = u - X -> staging tile; u tile <- v_new * exp(g_last - g_t)
       {
         float xr[kVT];
-        tmem_ld32(tX + lane_off, xr);
-        tmem_ld32(tX + lane_off + 32, xr + 32);
+        tmem_ld64(tX + lane_off, xr);  // one 64-column load, one wait
         if (lane < 16) {
           const int t = warp * 16 + lane;
           const float dec = __expf(gl - gc[t]);
@@ -332,8 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // S = exp(g_last) S + U_c
     {
       float ur[kVT];
-      tmem_ld32(tU + lane_off, ur);
-      tmem_ld32(tU + lane_off + 32, ur + 32);
+      tmem_ld64(tU + lane_off, ur);
       const float eg = __expf(gl);
       if (srow_ok) {
 #pragma unroll
