@@ -362,7 +362,8 @@ __global__ void __launch_bounds__(kBsdThreads) conv_bsd_generic(const T* __restr
 
 // ---------------------------------------------------------------------------
 // BSD through TMA tiles (D * sizeof(T) % 16 == 0, W <= 8): one CTA = 256
-// channels x a 256-step strip, tiles of 32 rows. Each tile and its W-1 halo
+// channels x a strip of STRIP steps (256, or 512 for large grids: see
+// long_strips), tiles of 32 rows. Each tile and its W-1 halo
 // rows arrive by TMA from a per-batch 3-D map [B][S][D] (rows before t = 0 are
 // the map's zero fill), 3-stage ring; the output tile is staged in smem and
 // written by TMA store. 256 threads: thread = 4 channels x 8 rows; a warp
@@ -373,7 +374,8 @@ namespace tma {
 constexpr int kThreads = 256;
 constexpr int kCh = 256;     // channels per CTA
 constexpr int kRows = 32;    // output rows per tile
-constexpr int kStrip = 256;  // rows per CTA
+constexpr int kStrip = 256;  // rows per CTA (kLongStrip for large grids)
+constexpr int kLongStrip = 512;
 constexpr int kStages = 2;
 
 template <typename T, int W>
@@ -387,6 +389,18 @@ struct Layout {
   static constexpr int OFF_BAR = OFF_OUT + 2 * OUT_BYTES;
   static constexpr int SMEM = OFF_BAR + 64 + 1024;
 };
+
+// Strip length for a launch. Each CTA pays a fixed start (barriers, weights,
+// the first TMA round trip), so longer strips stream more bytes per start; but a
+// grid of few waves (3 CTAs per SM) loses more to its last, partly filled wave
+// than it saves. Measured at T = 8192, D = 2048, bf16 (µs for one conv):
+// B = 16: 191.7 with 256-row strips, 185.6 with 512, 187.6 with 1024;
+// B = 8: 100.7 / 98.8 / 111.2; B = 4: 54.4 / 59.9 / 60.2; B = 2: 33.6 / 33.6 / 42.0.
+// So 512 rows where that grid still fills at least two waves, else 256.
+inline bool long_strips(int B, int D, int S) {
+  const long long ctas = (long long)((D + kCh - 1) / kCh) * B * ((S + kLongStrip - 1) / kLongStrip);
+  return ctas >= 2LL * 3 * sm_count();
+}
 
 // One row of the thread's 4 channels: shared memory <-> fp32 registers.
 template <typename T>
@@ -421,7 +435,7 @@ __device__ __forceinline__ float silu_tanh(float x) {
   return fmaf(h, t, h);
 }
 
-template <typename T, int W, bool SILU, int GL>
+template <typename T, int W, bool SILU, int GL, int STRIP>
 __global__ void __launch_bounds__(kThreads, 3)
     conv_bsd_tma(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_o,
                  const float* __restrict__ w, const float* __restrict__ bias, int S, int D) {
@@ -435,9 +449,9 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int tid = threadIdx.x;
   const int cg = tid % NCG, rq = tid / NCG;  // channel group, row band
   const int c0 = blockIdx.x * kCh;
-  const int t_begin = blockIdx.y * kStrip;
+  const int t_begin = blockIdx.y * STRIP;
   const int b = blockIdx.z;
-  const int ntiles = min(kStrip, S - t_begin + kRows - 1) / kRows;
+  const int ntiles = min(STRIP, S - t_begin + kRows - 1) / kRows;
   const int cc = min(c0 + C * cg, D - C);  // clamp: channels past D are computed but not stored
 
   float wr[C][W], bs[C];
@@ -584,10 +598,12 @@ int launch_bsd_tma(const T* x, const float* w, const float* b, T* o, int B, int 
   int r = encode_tiled(&tx, dt, 3, x, dims, str, ibox, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (r == THM_OK) r = encode_tiled(&to, dt, 3, o, dims, str, obox, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (r != THM_OK) return r;
-  auto kern = tma::conv_bsd_tma<T, W, SILU, GL>;
+  const bool lng = tma::long_strips(B, D, S);
+  auto kern = lng ? tma::conv_bsd_tma<T, W, SILU, GL, tma::kLongStrip> : tma::conv_bsd_tma<T, W, SILU, GL, tma::kStrip>;
+  const int strip = lng ? tma::kLongStrip : tma::kStrip;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
     return THM_ERR_CUDA;
-  dim3 grid((D + tma::kCh - 1) / tma::kCh, (S + tma::kStrip - 1) / tma::kStrip, B);
+  dim3 grid((D + tma::kCh - 1) / tma::kCh, (S + strip - 1) / strip, B);
   kern<<<grid, tma::kThreads, Ly::SMEM, st>>>(tx, to, w, b, S, D);
   return check_launch();
 }
