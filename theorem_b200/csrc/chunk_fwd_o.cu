@@ -406,9 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int hh = u % H, bc = u / H, c = bc % NT, b = bc / NT;
       const int row0 = b * T_len + c * 64;
-      float* gs = sGate + st * 64;
-      gs[lane] = g[(long long)(row0 + lane) * H + hh];
-      gs[lane + 32] = g[(long long)(row0 + lane + 32) * H + hh];
+      // the tiles first, so the gates' global-load round trip does not delay them
       if (lane == 0) {
         uint8_t* stg = sm + st * Ly::STAGE;
         mbar_arrive_expect_tx(&full[st], Ly::STAGE);
@@ -424,6 +422,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(stg + Ly::OFF_H + j * K * 128, &tm_h, &full[st], j * 64, hrow);
         }
       }
+      __syncwarp();
+      float* gs = sGate + st * 64;
+      gs[lane] = g[(long long)(row0 + lane) * H + hh];
+      gs[lane + 32] = g[(long long)(row0 + lane + 32) * H + hh];
       mbar_arrive(&full[st]);
     }
   } else if (warp == 1) {
@@ -706,9 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int vt = u % NVT, r = u / NVT, hh = r % H, bc = r / H, c = bc % NT, b = bc / NT;
       const int row0 = b * T_len + c * 64;
-      float* gs = sGate + st * 64;
-      gs[lane] = g[(long long)(row0 + lane) * H + hh];
-      gs[lane + 32] = g[(long long)(row0 + lane + 32) * H + hh];
+      // the tiles first, so the gates' global-load round trip does not delay them
       if (lane == 0) {
         uint8_t* stg = sm + st * Ly::STAGE;
         mbar_arrive_expect_tx(&full[st], Ly::STAGE);
@@ -720,6 +720,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(stg + Ly::OFF_V, &tm_v, &full[st], vt * kVT, hh, row0);
         tma_load_2d(stg + Ly::OFF_H32, &tm_h, &full[st], vt * kVT, ((b * NT + c) * H + hh) * K);
       }
+      __syncwarp();
+      float* gs = sGate + st * 64;
+      gs[lane] = g[(long long)(row0 + lane) * H + hh];
+      gs[lane + 32] = g[(long long)(row0 + lane + 32) * H + hh];
       mbar_arrive(&full[st]);
     }
   } else if (warp == 1) {
