@@ -6,7 +6,7 @@
 Headline (BASELINE.json metric "per-op us + %HBM / %TC peak; chained fwd
 tokens/s at 1/2/4/8 B200"): one step = one chained gated-DeltaNet layer
 forward at BASELINE config 5 (B=16, T=8192, H=16, K=V=128, D=2048, W=4, bf16):
-causal_conv1d(+SiLU, +L2 norm) on the q and k projections -> recompute_w_u with
+causal_conv1d(+SiLU, +L2 norm) on the q and k projections (one launch for both) -> recompute_w_u with
 the v projection's conv+SiLU folded in (in-kernel WY solve; v never reaches HBM)
 -> chunk_fwd_h (delta rule) + chunk_fwd_o as one fused kernel (``--unfused``: the
 v conv, recompute_w_u, chunk_fwd_h and chunk_fwd_o as separate launches). The 16
@@ -163,7 +163,9 @@ def chain_bytes(B, T, H, K, V, W):
     act_k, act_v = rows * K * 2, rows * V * 2
     hbytes = B * NT * H * K * V * 2
     return {
-        "causal_conv1d": 2 * act_k + H * K * (W + 1) * 4,          # one of q / k (v: same with V)
+        "causal_conv1d": 2 * act_k + H * K * (W + 1) * 4,          # one of q / k
+        "causal_conv1d_pair": 2 * (2 * act_k + H * K * (W + 1) * 4),  # q and k in one launch
+        "causal_conv1d_v": 2 * act_v + H * V * (W + 1) * 4,          # the v conv (separate-kernel path)
         "recompute_w_u": 2 * act_k + 2 * act_v + 2 * rows * 4,      # k,v in; w,u out; beta,g
         # k, raw v projection in; w, u out; beta, g; the v conv's weights (v never stored)
         "recompute_w_u_conv": 2 * act_k + 2 * act_v + 2 * rows * 4 + H * V * (W + 1) * 4,
@@ -206,9 +208,9 @@ def run_chain(args, rank, world, device, B, steps, sample_clocks=True):
     layer = GatedDeltaNetForward(H, K, V, cw, cb, fused=not args.unfused)
     fused = layer.uses_fused(torch.bfloat16)
     assert fused == layer.folds_v_conv(torch.bfloat16), "config 5's conv width is 4"
-    names = (("causal_conv1d_x2", "recompute_w_u_conv", "gated_delta_ho") if fused else
-             ("causal_conv1d_x3", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"))
-    launches = 4 if fused else 6
+    names = (("causal_conv1d_pair", "recompute_w_u_conv", "gated_delta_ho") if fused else
+             ("causal_conv1d_pair", "causal_conv1d_v", "recompute_w_u", "chunk_fwd_h", "chunk_fwd_o"))
+    launches = len(names)  # one launch each
     o = torch.empty(B, T, H, V, device=device, dtype=torch.bfloat16)
     stream = torch.cuda.current_stream()
 
@@ -220,8 +222,8 @@ def run_chain(args, rank, world, device, B, steps, sample_clocks=True):
         from theorem_b200 import ops
         bf = layer._buffers(xq, xv, B, T)
         evs[0].record(stream)
-        ops.causal_conv1d(xq, layer.wq, layer.bq, "silu", "bsd", K, out=bf["q"].view(B, T, H * K))
-        ops.causal_conv1d(xk, layer.wk, layer.bk, "silu", "bsd", K, out=bf["k"].view(B, T, H * K))
+        ops.causal_conv1d_pair(xq, layer.wq, layer.bq, xk, layer.wk, layer.bk, "silu", K,
+                               out0=bf["q"].view(B, T, H * K), out1=bf["k"].view(B, T, H * K))
         if fused:
             evs[1].record(stream)
             w, u = ops.recompute_w_u_conv(bf["k"], xv, layer.wv, layer.bv, beta, gate, "silu", a_mode=1,
@@ -230,14 +232,15 @@ def run_chain(args, rank, world, device, B, steps, sample_clocks=True):
             ops.gated_delta_fwd_ho(bf["q"], bf["k"], w, u, gate, layer.scale, o=o)
             evs[3].record(stream)
             return
-        ops.causal_conv1d(xv, layer.wv, layer.bv, "silu", "bsd", 0, out=bf["v"].view(B, T, H * V))
         evs[1].record(stream)
-        w, u = ops.recompute_w_u(bf["k"], bf["v"], beta, None, gate, a_mode=1, w=bf["w"], u=bf["u"])
+        ops.causal_conv1d(xv, layer.wv, layer.bv, "silu", "bsd", 0, out=bf["v"].view(B, T, H * V))
         evs[2].record(stream)
-        h, vn, _ = ops.chunk_fwd_h(bf["k"], u, gate, w=w, mode=1, h=bf["h"], v_new=bf["v"])
+        w, u = ops.recompute_w_u(bf["k"], bf["v"], beta, None, gate, a_mode=1, w=bf["w"], u=bf["u"])
         evs[3].record(stream)
-        ops.chunk_fwd_o(bf["q"], bf["k"], vn, gate, h, layer.scale, o=o)
+        h, vn, _ = ops.chunk_fwd_h(bf["k"], u, gate, w=w, mode=1, h=bf["h"], v_new=bf["v"])
         evs[4].record(stream)
+        ops.chunk_fwd_o(bf["q"], bf["k"], vn, gate, h, layer.scale, o=o)
+        evs[5].record(stream)
 
     sampler = ClockSampler(device.index) if rank == 0 and sample_clocks else None
     if sampler:
@@ -762,8 +765,7 @@ def main(argv=None) -> int:
     value = B * T / (ms / 1e3)
     by = chain_bytes(Bl, T, H, K, V, W)
     per_ms = res["per_op_ms"]
-    per_launch = {("causal_conv1d" if n.startswith("causal_conv1d_x") else n):
-                  (v / int(n[-1]) if n.startswith("causal_conv1d_x") else v) for n, v in per_ms.items()}
+    per_launch = per_ms  # every entry is one launch
     dom = max(per_launch, key=lambda n: per_launch[n])
     dom_ms = per_launch[dom]
     achieved = by[dom] / (dom_ms * 1e-3) / 1e9
@@ -771,11 +773,7 @@ def main(argv=None) -> int:
     tf = ROOT / "profiles" / "dram_traffic.json"
     if tf.exists() and world == 1:
         traffic = json.loads(tf.read_text()).get(f"chain_{dom}")
-    # q, k convs; the v conv as its own launch only on the unfused path
-    chain_step_bytes = 2 * by["causal_conv1d"] + sum(by[n] for n in per_ms if n in (
-        "recompute_w_u", "recompute_w_u_conv", "chunk_fwd_h", "chunk_fwd_o", "gated_delta_ho"))
-    if not res["fused"]:
-        chain_step_bytes += 2 * Bl * T * H * V * 2 + H * V * (W + 1) * 4
+    chain_step_bytes = sum(by[n] for n in per_ms)
     flops = chain_flops(Bl, T, H, K, V)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,

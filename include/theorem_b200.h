@@ -59,6 +59,20 @@ int thm_causal_conv1d_fwd(const void* x, const float* weight, const float* bias,
                           thm_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * causal_conv1d on two inputs of the same shape in one launch -- no reference
+ * counterpart of its own: it is thm_causal_conv1d_fwd (THM_LAYOUT_BSD) applied
+ * to (x0, weight0, bias0) -> out0 and to (x1, weight1, bias1) -> out1, with the
+ * same B, D, S, W, dtype, activation and l2norm_group, and results bit-identical
+ * to those two calls. The gated-DeltaNet layer runs its q and k projections'
+ * convs this way: one grid of 2B sequences wastes less on its last, partly filled
+ * wave than two grids of B. Where the TMA path does not apply (D * elem % 16 != 0,
+ * W not in {2,3,4}) it issues the two single-conv launches.
+ * ------------------------------------------------------------------------- */
+int thm_causal_conv1d_pair_fwd(const void* x0, const float* weight0, const float* bias0, void* out0,
+                               const void* x1, const float* weight1, const float* bias1, void* out1, int B, int D,
+                               int S, int W, int dtype, int activation, int l2norm_group, thm_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * recompute_w_u -- replaces kernels/recompute_w_u/kernel.py:192-248
  * (_launch / custom_kernel; Triton recompute_w_u_kernel :73-186).
  *

@@ -57,6 +57,26 @@ def test_invalid_arguments_rejected_without_gpu():
     assert lib.thm_causal_conv1d_fwd(None, None, None, None, 1, 8, 8, 4, 7, 0, 0, 0, None) == _lib.THM_ERR_INVALID
 
 
+def test_conv_pair_rejects_arguments_without_gpu():
+    """thm_causal_conv1d_pair_fwd checks its arguments on the host, before any CUDA
+    call; an empty problem is a no-op."""
+    lib = _lib.load()
+    f = lib.thm_causal_conv1d_pair_fwd
+    fake = 1 << 20  # never dereferenced: every case returns before touching memory
+    p8 = [fake] * 8
+    assert f(*p8, 1, 8, 8, 0, 1, 1, 0, None) == _lib.THM_ERR_INVALID          # W = 0
+    assert f(*([None] * 8), 0, 8, 8, 4, 1, 1, 0, None) == _lib.THM_OK         # empty batch
+    assert f(*([None] * 8), 1, 8, 8, 4, 1, 1, 0, None) == _lib.THM_ERR_INVALID  # null pointers
+    assert f(*p8, 1, 8, 8, 4, 1, 7, 0, None) == _lib.THM_ERR_INVALID          # unknown activation
+    assert f(*p8, 1, 8, 8, 4, 9, 1, 0, None) == _lib.THM_ERR_INVALID          # unknown dtype
+    assert f(*p8, 1, 6, 8, 4, 1, 1, 0, None) == _lib.THM_ERR_UNSUPPORTED      # D % 4 != 0
+    assert f(*p8, 1, 8, 8, 65, 1, 1, 0, None) == _lib.THM_ERR_UNSUPPORTED     # W > 64
+    assert f(*p8, 1, 8, 8, 4, 1, 1, 16, None) == _lib.THM_ERR_INVALID         # group does not divide D
+    assert f(*p8, 1, 48, 8, 4, 1, 1, 24, None) == _lib.THM_ERR_UNSUPPORTED    # group size not built
+    bad = [fake + 4] + [fake] * 7
+    assert f(*bad, 1, 8, 8, 4, 1, 1, 0, None) == _lib.THM_ERR_ALIGNMENT       # x0 not 16-byte aligned
+
+
 def test_conv_folded_recompute_w_u_rejects_arguments_without_gpu():
     """thm_recompute_w_u_conv_fwd checks its arguments on the host, before any CUDA call:
     only an in-kernel A (a_mode +1 / -1), a known activation, T % 64 == 0, and conv

@@ -31,6 +31,7 @@ _F = ctypes.c_float
 
 _SIGNATURES = {
     "thm_causal_conv1d_fwd": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P],
+    "thm_causal_conv1d_pair_fwd": [_P] * 8 + [_I] * 7 + [_P],
     "thm_recompute_w_u_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
     "thm_chunk_fwd_h_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P],
     "thm_chunk_fwd_o_fwd": [_P, _P, _P, _P, _P, _P, _F, _I, _I, _I, _I, _I, _I, _I, _P],

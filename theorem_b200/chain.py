@@ -79,8 +79,8 @@ class GatedDeltaNetForward:
         assert T % 64 == 0, "T must be a multiple of the chunk length 64"
         bf = self._buffers(xq, xv, B, T)
         q, k, v = bf["q"], bf["k"], bf["v"]
-        ops.causal_conv1d(xq, self.wq, self.bq, self.activation, "bsd", K, out=q.view(B, T, H * K))
-        ops.causal_conv1d(xk, self.wk, self.bk, self.activation, "bsd", K, out=k.view(B, T, H * K))
+        ops.causal_conv1d_pair(xq, self.wq, self.bq, xk, self.wk, self.bk, self.activation, K,
+                               out0=q.view(B, T, H * K), out1=k.view(B, T, H * K))
         if self.folds_v_conv(xq.dtype):
             w, u = ops.recompute_w_u_conv(k, xv, self.wv, self.bv, beta, g, self.activation, a_mode=1,
                                           w=bf["w"], u=bf["u"])

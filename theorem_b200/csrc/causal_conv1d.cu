@@ -435,10 +435,11 @@ __device__ __forceinline__ float silu_tanh(float x) {
   return fmaf(h, t, h);
 }
 
+// One CTA's strip of one sequence b (the body of both kernels below).
 template <typename T, int W, bool SILU, int GL, int STRIP>
-__global__ void __launch_bounds__(kThreads, 3)
-    conv_bsd_tma(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_o,
-                 const float* __restrict__ w, const float* __restrict__ bias, int S, int D) {
+__device__ __forceinline__ void bsd_tma_strip(const CUtensorMap* tm_x, const CUtensorMap* tm_o,
+                                              const float* __restrict__ w, const float* __restrict__ bias, int S,
+                                              int D, int b) {
   using Ly = Layout<T, W>;
   constexpr int C = 4;                           // channels per thread
   constexpr int NCG = kCh / C;                   // channel groups across the 256 channels
@@ -450,7 +451,6 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int cg = tid % NCG, rq = tid / NCG;  // channel group, row band
   const int c0 = blockIdx.x * kCh;
   const int t_begin = blockIdx.y * STRIP;
-  const int b = blockIdx.z;
   const int ntiles = min(STRIP, S - t_begin + kRows - 1) / kRows;
   const int cc = min(c0 + C * cg, D - C);  // clamp: channels past D are computed but not stored
 
@@ -469,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   auto issue = [&](int i) {
     const int st = i % kStages;
     mbar_arrive_expect_tx(&full[st], Ly::IN_ROWS * kCh * Ly::ES);
-    tma_load_3d(sm + st * Ly::IN_STRIDE, &tm_x, &full[st], c0, t_begin + i * kRows - (W - 1), b);
+    tma_load_3d(sm + st * Ly::IN_STRIDE, tm_x, &full[st], c0, t_begin + i * kRows - (W - 1), b);
   };
   if (tid == 0)
     for (int i = 0; i < kStages && i < ntiles; ++i) issue(i);
@@ -532,12 +532,34 @@ __global__ void __launch_bounds__(kThreads, 3)
     fence_proxy_async_smem();
     __syncthreads();
     if (tid == 0) {
-      tma_store_3d(&tm_o, out, c0, t_begin + i * kRows, b);
+      tma_store_3d(tm_o, out, c0, t_begin + i * kRows, b);
       bulk_commit_group();
       if (i + kStages < ntiles) issue(i + kStages);
     }
   }
   if (tid == 0) bulk_wait_group0();
+}
+
+template <typename T, int W, bool SILU, int GL, int STRIP>
+__global__ void __launch_bounds__(kThreads, 3)
+    conv_bsd_tma(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_o,
+                 const float* __restrict__ w, const float* __restrict__ bias, int S, int D) {
+  bsd_tma_strip<T, W, SILU, GL, STRIP>(&tm_x, &tm_o, w, bias, S, D, blockIdx.z);
+}
+
+// Two convs of the same shape in one grid (the layer's q and k projections):
+// blockIdx.z < B is sequence z of the first, else sequence z - B of the second.
+// One grid of 2B sequences has half as many partly filled last waves as two
+// launches of B, which matters when B is small.
+template <typename T, int W, bool SILU, int GL, int STRIP>
+__global__ void __launch_bounds__(kThreads, 3)
+    conv_bsd_tma_pair(const __grid_constant__ CUtensorMap tm_x0, const __grid_constant__ CUtensorMap tm_o0,
+                      const float* __restrict__ w0, const float* __restrict__ bias0,
+                      const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_o1,
+                      const float* __restrict__ w1, const float* __restrict__ bias1, int S, int D, int B) {
+  const bool second = (int)blockIdx.z >= B;
+  bsd_tma_strip<T, W, SILU, GL, STRIP>(second ? &tm_x1 : &tm_x0, second ? &tm_o1 : &tm_o0, second ? w1 : w0,
+                                       second ? bias1 : bias0, S, D, (int)blockIdx.z - (second ? B : 0));
 }
 }  // namespace tma
 
@@ -608,6 +630,32 @@ int launch_bsd_tma(const T* x, const float* w, const float* b, T* o, int B, int 
   return check_launch();
 }
 
+template <typename T, int W, bool SILU, int GL>
+int launch_bsd_tma_pair(const T* x0, const float* w0, const float* b0, T* o0, const T* x1, const float* w1,
+                        const float* b1, T* o1, int B, int D, int S, cudaStream_t st) {
+  using Ly = tma::Layout<T, W>;
+  const CUtensorMapDataType dt = sizeof(T) == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUtensorMap tx0, to0, tx1, to1;
+  uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)B};
+  uint64_t str[2] = {(uint64_t)D * sizeof(T), (uint64_t)S * D * sizeof(T)};
+  uint32_t ibox[3] = {(uint32_t)tma::kCh, (uint32_t)Ly::IN_ROWS, 1u};
+  uint32_t obox[3] = {(uint32_t)tma::kCh, (uint32_t)tma::kRows, 1u};
+  int r = encode_tiled(&tx0, dt, 3, x0, dims, str, ibox, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (r == THM_OK) r = encode_tiled(&to0, dt, 3, o0, dims, str, obox, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (r == THM_OK) r = encode_tiled(&tx1, dt, 3, x1, dims, str, ibox, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (r == THM_OK) r = encode_tiled(&to1, dt, 3, o1, dims, str, obox, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (r != THM_OK) return r;
+  const bool lng = tma::long_strips(2 * B, D, S);
+  auto kern = lng ? tma::conv_bsd_tma_pair<T, W, SILU, GL, tma::kLongStrip>
+                  : tma::conv_bsd_tma_pair<T, W, SILU, GL, tma::kStrip>;
+  const int strip = lng ? tma::kLongStrip : tma::kStrip;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Ly::SMEM) != cudaSuccess)
+    return THM_ERR_CUDA;
+  dim3 grid((D + tma::kCh - 1) / tma::kCh, (S + strip - 1) / strip, 2 * B);
+  kern<<<grid, tma::kThreads, Ly::SMEM, st>>>(tx0, to0, w0, b0, tx1, to1, w1, b1, S, D, B);
+  return check_launch();
+}
+
 template <typename T, bool SILU, int GL>
 int dispatch_bsd_w(const T* x, const float* w, const float* b, T* o, int B, int D, int S, int W,
                    cudaStream_t st) {
@@ -639,6 +687,35 @@ int dispatch_bsd(const T* x, const float* w, const float* b, T* o, int B, int D,
     case 32: return dispatch_bsd_w<T, SILU, 8>(x, w, b, o, B, D, S, W, st);
     case 64: return dispatch_bsd_w<T, SILU, 16>(x, w, b, o, B, D, S, W, st);
     case 128: return dispatch_bsd_w<T, SILU, 32>(x, w, b, o, B, D, S, W, st);
+    default: return THM_ERR_UNSUPPORTED;
+  }
+}
+
+// Both convs in one launch where the TMA path applies (one grid of 2B sequences),
+// else as two launches of the single-conv path.
+template <typename T, bool SILU, int GL>
+int dispatch_bsd_pair_w(const T* x0, const float* w0, const float* b0, T* o0, const T* x1, const float* w1,
+                        const float* b1, T* o1, int B, int D, int S, int W, cudaStream_t st) {
+  if ((D * (int)sizeof(T)) % 16 == 0 && D >= 4 && (W == 2 || W == 3 || W == 4) && 2LL * B <= 65535) {
+    switch (W) {
+      case 2: return launch_bsd_tma_pair<T, 2, SILU, GL>(x0, w0, b0, o0, x1, w1, b1, o1, B, D, S, st);
+      case 3: return launch_bsd_tma_pair<T, 3, SILU, GL>(x0, w0, b0, o0, x1, w1, b1, o1, B, D, S, st);
+      default: return launch_bsd_tma_pair<T, 4, SILU, GL>(x0, w0, b0, o0, x1, w1, b1, o1, B, D, S, st);
+    }
+  }
+  const int r = dispatch_bsd_w<T, SILU, GL>(x0, w0, b0, o0, B, D, S, W, st);
+  return r != THM_OK ? r : dispatch_bsd_w<T, SILU, GL>(x1, w1, b1, o1, B, D, S, W, st);
+}
+
+template <typename T, bool SILU>
+int dispatch_bsd_pair(const T* x0, const float* w0, const float* b0, T* o0, const T* x1, const float* w1,
+                      const float* b1, T* o1, int B, int D, int S, int W, int G, cudaStream_t st) {
+  switch (G) {
+    case 0: return dispatch_bsd_pair_w<T, SILU, 0>(x0, w0, b0, o0, x1, w1, b1, o1, B, D, S, W, st);
+    case 16: return dispatch_bsd_pair_w<T, SILU, 4>(x0, w0, b0, o0, x1, w1, b1, o1, B, D, S, W, st);
+    case 32: return dispatch_bsd_pair_w<T, SILU, 8>(x0, w0, b0, o0, x1, w1, b1, o1, B, D, S, W, st);
+    case 64: return dispatch_bsd_pair_w<T, SILU, 16>(x0, w0, b0, o0, x1, w1, b1, o1, B, D, S, W, st);
+    case 128: return dispatch_bsd_pair_w<T, SILU, 32>(x0, w0, b0, o0, x1, w1, b1, o1, B, D, S, W, st);
     default: return THM_ERR_UNSUPPORTED;
   }
 }
@@ -682,4 +759,38 @@ extern "C" int thm_causal_conv1d_fwd(const void* x, const float* weight, const f
   auto of = static_cast<float*>(out);
   return silu ? dispatch_bsd<float, true>(xf, weight, bias, of, B, D, S, W, l2norm_group, st)
               : dispatch_bsd<float, false>(xf, weight, bias, of, B, D, S, W, l2norm_group, st);
+}
+
+extern "C" int thm_causal_conv1d_pair_fwd(const void* x0, const float* weight0, const float* bias0, void* out0,
+                                          const void* x1, const float* weight1, const float* bias1, void* out1,
+                                          int B, int D, int S, int W, int dtype, int activation, int l2norm_group,
+                                          thm_stream_t stream) {
+  using namespace thm;
+  using namespace thm::conv;
+  if (B < 0 || D < 0 || S < 0 || W < 1) return THM_ERR_INVALID;
+  if (activation != THM_ACT_NONE && activation != THM_ACT_SILU) return THM_ERR_INVALID;
+  if (dtype != THM_F32 && dtype != THM_BF16) return THM_ERR_INVALID;
+  if ((long long)B * D * S == 0) return THM_OK;  // empty tensors: nothing to do
+  if (!x0 || !weight0 || !bias0 || !out0 || !x1 || !weight1 || !bias1 || !out1) return THM_ERR_INVALID;
+  if (W > 64) return THM_ERR_UNSUPPORTED;
+  if (D % 4 != 0) return THM_ERR_UNSUPPORTED;
+  if (!aligned16(x0) || !aligned16(out0) || !aligned16(x1) || !aligned16(out1)) return THM_ERR_ALIGNMENT;
+  if (l2norm_group != 0 && D % l2norm_group != 0) return THM_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool silu = activation == THM_ACT_SILU;
+  if (dtype == THM_BF16) {
+    using bf = __nv_bfloat16;
+    auto a0 = static_cast<const bf*>(x0);
+    auto a1 = static_cast<const bf*>(x1);
+    auto p0 = static_cast<bf*>(out0);
+    auto p1 = static_cast<bf*>(out1);
+    return silu ? dispatch_bsd_pair<bf, true>(a0, weight0, bias0, p0, a1, weight1, bias1, p1, B, D, S, W, l2norm_group, st)
+                : dispatch_bsd_pair<bf, false>(a0, weight0, bias0, p0, a1, weight1, bias1, p1, B, D, S, W, l2norm_group, st);
+  }
+  auto a0 = static_cast<const float*>(x0);
+  auto a1 = static_cast<const float*>(x1);
+  auto p0 = static_cast<float*>(out0);
+  auto p1 = static_cast<float*>(out1);
+  return silu ? dispatch_bsd_pair<float, true>(a0, weight0, bias0, p0, a1, weight1, bias1, p1, B, D, S, W, l2norm_group, st)
+              : dispatch_bsd_pair<float, false>(a0, weight0, bias0, p0, a1, weight1, bias1, p1, B, D, S, W, l2norm_group, st);
 }

@@ -77,6 +77,39 @@ def causal_conv1d(x, weight, bias, activation=None, layout: str = "bds", l2norm_
 
 
 @_on_input_device
+def causal_conv1d_pair(x0, weight0, bias0, x1, weight1, bias1, activation=None, l2norm_group: int = 0,
+                       out0=None, out1=None):
+    """Two channel-last convs of the same shape in one launch (the layer's q and k
+    projections): equal bit for bit to ``causal_conv1d(x0, weight0, bias0, activation,
+    "bsd", l2norm_group)`` and the same for x1. x0, x1 [B, S, D] fp32 or bf16 of one
+    dtype; weights [D, W] and biases [D] fp32. Returns (out0, out1)."""
+    _cuda(x0, weight0, bias0, x1, weight1, bias1, out0, out1)
+    _contig(x0, weight0, bias0, x1, weight1, bias1)
+    for t in (weight0, bias0, weight1, bias1):
+        assert t.dtype == torch.float32, "weight/bias must be float32"
+    assert x0.dim() == 3 and x1.shape == x0.shape, "x0, x1 must be [B, S, D] of one shape"
+    assert x1.dtype == x0.dtype and x1.device == x0.device, "x0, x1 must share dtype and device"
+    B, S, D = x0.shape
+    W = weight0.shape[1]
+    for wt, bt in ((weight0, bias0), (weight1, bias1)):
+        assert wt.shape == (D, W), f"weight shape {tuple(wt.shape)} != ({D}, {W})"
+        assert bt.shape == (D,), f"bias shape {tuple(bt.shape)} != ({D},)"
+    outs = []
+    for o in (out0, out1):
+        if o is None:
+            o = torch.empty_like(x0)
+        assert o.shape == x0.shape and o.dtype == x0.dtype and o.is_contiguous() and o.device == x0.device, \
+            "out must match x in shape, dtype and device and be contiguous"
+        outs.append(o)
+    st = L.stream_of(x0)
+    L.check(L.load().thm_causal_conv1d_pair_fwd(L.ptr(x0), L.ptr(weight0), L.ptr(bias0), L.ptr(outs[0]),
+                                                L.ptr(x1), L.ptr(weight1), L.ptr(bias1), L.ptr(outs[1]),
+                                                B, D, S, W, L.dtype_code(x0), _ACT[activation], int(l2norm_group), st),
+            "thm_causal_conv1d_pair_fwd")
+    return outs[0], outs[1]
+
+
+@_on_input_device
 def recompute_w_u(k, v, beta, A, g, a_mode: int = 0, w=None, u=None, A_out=None):
     """w = A (k beta e^g), u = A (v beta) per 64-chunk (kernels/recompute_w_u/kernel.py:192-248).
 
